@@ -1,0 +1,444 @@
+#!/usr/bin/env python
+"""Attention-forward benchmark (bf16, head dim 128, non-causal) on B200.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--config c2] [--impl ours|reference]
+
+One step = one forward over the configuration's inputs, already resident in
+HBM. Each timed launch is bracketed by CUDA events on the launching stream;
+L2 (126 MB) is flushed by a 256 MiB write between timed steps, outside the
+events. value = algorithmic FLOPs (4*B*H*Sq*Sk*128) of all ranks / the
+slowest rank's mean step time. With N > 1 ranks (torchrun, one per GPU):
+configurations with several heads are sharded over heads (no exchange in the
+data path; NCCL only gathers O afterwards when --validate is given); single
+(batch, head) configurations run one replica per GPU.
+
+`--impl reference` times the reference's own kernel (llm_fa.cu built from its
+sources into oracle/_ref/) through its own `llm_fa_forward` on rank 0, one 2-D
+launch per (batch, head), kernel durations from CUPTI (the reference launcher
+allocates O and synchronises the device inside every call, so events on the
+stream cannot bracket its kernel alone); when that module is absent it times
+the reference's CPU oracle path (fp32 SDPA, validate.py:19-27) instead.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import math
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+from datetime import timedelta
+from pathlib import Path
+
+ROOT = Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT))
+
+METRIC = "attn fwd TFLOP/s bf16 hd128 & % of tensor peak; µs vs llm_fa.cu/FA4 same box"
+UNIT = "TFLOP/s"
+# Reference's published TFLOP/s for the same shapes (ncu, SM clock locked
+# at ~1.07 GHz, computed from the published microseconds of llm_fa.cu).
+PUBLISHED_REF_TFLOPS = {"c2": 362.5, "c3": 810.6}
+# DRAM bytes per launch (dram__bytes_read.sum + dram__bytes_write.sum) from the ncu capture
+# summarised in profiles/; None until measured for that configuration.
+PROFILED_TRAFFIC_BYTES: dict[str, float | None] = {}
+L2_FLUSH_BYTES = 256 << 20
+
+
+def parse_args():
+    ap = argparse.ArgumentParser(description=__doc__.splitlines()[0])
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--config", default="c2", help="c1..c5 (BASELINE.json configs)")
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--validate", action="store_true", help="NCCL-gather O to rank 0 afterwards")
+    ap.add_argument("--cpu-seconds", type=float, default=10.0, help="CPU baseline sample budget")
+    return ap.parse_args()
+
+
+# ------------------------------------------------------------------ environment
+def dist_env():
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    return world, rank, local
+
+
+def measured_peaks() -> dict:
+    p = ROOT / "MEASURED_PEAKS.json"
+    if p.exists():
+        try:
+            return json.loads(p.read_text())
+        except Exception:
+            pass
+    return {}
+
+
+class ClockSampler:
+    """nvidia-smi samples (200 ms) of one GPU while the timed region runs."""
+
+    FIELDS = ("clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, index: int):
+        self.index = index
+        self.proc = None
+        self.lines: list[str] = []
+        self.thread = None
+
+    def start(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--id={self.index}", f"--query-gpu={self.FIELDS}",
+                 "--format=csv,noheader,nounits", "-lms", "200"],
+                stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+        except (OSError, ValueError):
+            self.proc = None
+            return
+        self.thread = threading.Thread(target=self._read, daemon=True)
+        self.thread.start()
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.lines.append(line.strip())
+
+    def stop(self) -> dict | None:
+        if self.proc is None:
+            return None
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except subprocess.TimeoutExpired:
+            self.proc.kill()
+        if self.thread is not None:
+            self.thread.join(timeout=2)
+        sm, mx, reasons = [], [], set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for ln in self.lines:
+            parts = [x.strip() for x in ln.split(",")]
+            if len(parts) < 8:
+                continue
+            try:
+                sm.append(float(parts[0]))
+                mx.append(float(parts[1]))
+            except ValueError:
+                continue
+            for nm, val in zip(names, parts[4:8]):
+                if val.lower() == "active":
+                    reasons.add(nm)
+        if not sm:
+            return None
+        return {"sm_mhz": statistics.median(sm), "sm_max_mhz": max(mx), "reasons": sorted(reasons),
+                "samples": len(sm)}
+
+
+# ------------------------------------------------------------------ workload
+def local_shard(cfg, world: int, rank: int):
+    """Which part of the workload this rank runs: ('heads', h0, h1), ('batch', b0, b1) or
+    ('replica',)."""
+    if world == 1:
+        return ("all",)
+    if cfg.heads % world == 0:
+        hs = cfg.heads // world
+        return ("heads", rank * hs, (rank + 1) * hs)
+    if cfg.batch % world == 0:
+        bs = cfg.batch // world
+        return ("batch", rank * bs, (rank + 1) * bs)
+    return ("replica",)
+
+
+def slice_inputs(q, k, v, shard):
+    if shard[0] == "heads":
+        return tuple(t[:, :, shard[1]:shard[2]].contiguous() for t in (q, k, v))
+    if shard[0] == "batch":
+        return tuple(t[shard[1]:shard[2]].contiguous() for t in (q, k, v))
+    return q, k, v
+
+
+def cpu_baseline(cfg, budget_s: float) -> dict:
+    """The reference's oracle path (fp32 SDPA, validate.py:19-27) on host cores, on a
+    seeded subset of query rows of one head (rows are independent)."""
+    import torch
+
+    from llm_fa_b200.workloads import make_inputs, sample_rows
+    from oracle.sdpa_oracle import sdpa_fp32
+
+    threads = os.cpu_count() or 1
+    torch.set_num_threads(threads)
+    g = torch.Generator().manual_seed(cfg.seed)
+    # one (batch, head) slice of the workload's shape, same distribution
+    small = type(cfg)(cfg.name, 1, 1, cfg.seq_q, cfg.seq_k, cfg.seed, cfg.stress_rows)
+    q, k, v = make_inputs(small) if cfg.seq_q * cfg.seq_k <= (1 << 34) else (
+        torch.randn(1, cfg.seq_q, 1, 128, generator=g).bfloat16(),
+        torch.randn(1, cfg.seq_k, 1, 128, generator=g).bfloat16(),
+        torch.randn(1, cfg.seq_k, 1, 128, generator=g).bfloat16())
+    rows = sample_rows(small, 64)
+    sdpa_fp32(q, k, v, rows=rows)  # warm-up
+    t0 = time.perf_counter()
+    sdpa_fp32(q, k, v, rows=rows)
+    t_one = max(time.perf_counter() - t0, 1e-4)
+    n = int(min(cfg.seq_q, max(64, 64 * budget_s / 3.0 / t_one)))
+    rows = sample_rows(small, n)
+    reps, total = 0, 0.0
+    while total < budget_s * 0.66 or reps < 1:
+        t0 = time.perf_counter()
+        sdpa_fp32(q, k, v, rows=rows)
+        total += time.perf_counter() - t0
+        reps += 1
+        if reps >= 3:
+            break
+    t = total / reps
+    flops = 4.0 * len(rows) * cfg.seq_k * 128
+    return {"value": flops / t / 1e12, "unit": UNIT, "cores": threads, "kind": "port",
+            "sample": f"fp32 SDPA (torch CPU) on {len(rows)} seeded query rows x {cfg.seq_k} keys "
+                      f"of one head, {reps} reps, {t:.2f} s/rep; TFLOP/s of that sample"}
+
+
+# ------------------------------------------------------------------ our arm
+def run_ours(args, cfg, world, rank, local):
+    import torch
+    import torch.distributed as dist
+
+    from llm_fa_b200 import attention_forward, device_status
+    from llm_fa_b200.workloads import make_inputs
+
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    shard = local_shard(cfg, world, rank)
+    q_h, k_h, v_h = slice_inputs(*make_inputs(cfg), shard)
+    B, Sq, H, _ = q_h.shape
+    Sk = k_h.shape[1]
+    flops_local = 4 * B * H * Sq * Sk * 128
+    q, k, v = q_h.to(dev), k_h.to(dev), v_h.to(dev)
+    o = torch.empty_like(q)
+    flush = torch.empty(L2_FLUSH_BYTES, dtype=torch.uint8, device=dev)
+    stream = torch.cuda.current_stream(dev)
+
+    def step():
+        attention_forward(q, k, v, out=o)
+
+    for _ in range(max(args.warmup, 3)):
+        step()
+    torch.cuda.synchronize(dev)
+    st = device_status(dev)
+    if st != 0:
+        raise RuntimeError(f"device status {st:#x} after warm-up")
+    if world > 1:
+        dist.barrier()
+    sampler = ClockSampler(local)
+    sampler.start()
+    time.sleep(0.3)
+    starts = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
+    ends = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
+    torch.cuda.synchronize(dev)
+    if world > 1:
+        dist.barrier()
+    for i in range(args.steps):
+        flush.zero_()
+        starts[i].record(stream)
+        step()
+        ends[i].record(stream)
+    torch.cuda.synchronize(dev)
+    if world > 1:
+        dist.barrier()
+    clocks = sampler.stop()
+    times_ms = [s.elapsed_time(e) for s, e in zip(starts, ends)]
+    mean_ms = statistics.fmean(times_ms)
+    st = device_status(dev)
+    if st != 0:
+        raise RuntimeError(f"device status {st:#x} after timed steps")
+
+    # end to end through the public API: pinned host inputs -> device -> O back to host
+    e2e = None
+    if not args.no_e2e:
+        qp, kp, vp = (t.pin_memory() for t in (q_h, k_h, v_h))
+        op = torch.empty(o.shape, dtype=o.dtype).pin_memory()
+        qd, kd, vd, od = (torch.empty_like(t) for t in (q, k, v, o))
+
+        def e2e_step():
+            qd.copy_(qp, non_blocking=True)
+            kd.copy_(kp, non_blocking=True)
+            vd.copy_(vp, non_blocking=True)
+            attention_forward(qd, kd, vd, out=od)
+            op.copy_(od, non_blocking=True)
+
+        for _ in range(max(args.warmup, 3)):
+            e2e_step()
+        torch.cuda.synchronize(dev)
+        if world > 1:
+            dist.barrier()
+        es = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
+        ee = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
+        for i in range(args.steps):
+            es[i].record(stream)
+            e2e_step()
+            ee[i].record(stream)
+        torch.cuda.synchronize(dev)
+        e2e_ms = statistics.fmean(s.elapsed_time(e) for s, e in zip(es, ee))
+        e2e = {"ms": e2e_ms, "h2d": sum(t.numel() * t.element_size() for t in (q_h, k_h, v_h)),
+               "d2h": o.numel() * o.element_size()}
+
+    # max over ranks
+    if world > 1:
+        t = torch.tensor([mean_ms, e2e["ms"] if e2e else 0.0], dtype=torch.float64, device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        mean_ms_max, e2e_ms_max = float(t[0]), float(t[1])
+        tot = torch.tensor([float(flops_local)], dtype=torch.float64, device=dev)
+        dist.all_reduce(tot)
+        flops_total = float(tot[0])
+        if args.validate:
+            gathered = [torch.empty_like(o) for _ in range(world)]
+            dist.all_gather(gathered, o)
+            if rank == 0:
+                ok = all(torch.isfinite(g.float()).all().item() for g in gathered)
+                print(f"# gathered O from {world} ranks over NCCL: finite={ok}", file=sys.stderr)
+    else:
+        mean_ms_max = mean_ms
+        e2e_ms_max = e2e["ms"] if e2e else 0.0
+        flops_total = float(flops_local)
+
+    if rank != 0:
+        return None
+    peaks = measured_peaks()
+    peak = peaks.get("bf16_tflops")
+    peak_src = "measured burst (MEASURED_PEAKS.json bf16_tflops)" if peak else "fallback 1590"
+    peak = float(peak) if peak else 1590.0
+    achieved = flops_local / (mean_ms / 1e3) / 1e12  # this rank's kernel, per launch
+    value = flops_total / (mean_ms_max / 1e3) / 1e12
+    line = {
+        "metric": METRIC, "value": round(value, 2), "unit": UNIT, "n_gpus": world,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(mean_ms_max, 5),
+        "higher_is_better": True,
+        "scaling": "strong" if shard[0] in ("heads", "batch") else "weak",
+        "vs_baseline": (round(value / world / PUBLISHED_REF_TFLOPS[cfg.name], 3)
+                        if cfg.name in PUBLISHED_REF_TFLOPS else None),
+        "dtype": "bf16", "data": "synthetic (seeded N(0,1) bf16 inputs, BASELINE.json shapes)",
+        "config": {"workload": f"{cfg.name}: {cfg.describe()} non-causal, scale 1/sqrt(128)",
+                   "global_batch": cfg.batch, "heads": cfg.heads, "seq_q": cfg.seq_q,
+                   "seq_k": cfg.seq_k, "head_dim": 128,
+                   "parallelism": {"all": "single GPU", "heads": f"heads sharded over {world} GPUs",
+                                   "batch": f"batch sharded over {world} GPUs",
+                                   "replica": f"{world} independent replicas"}[shard[0]],
+                   "l2": "flushed between timed steps (256 MiB write, outside the events)"},
+        "roofline": {"bound": "tensor", "achieved": round(achieved, 2), "peak": peak,
+                     "unit": "TFLOP/s", "frac": round(achieved / peak, 4),
+                     "peak_source": peak_src,
+                     "traffic": PROFILED_TRAFFIC_BYTES.get(cfg.name),
+                     "algorithmic_bytes": cfg.io_bytes},
+        "gpu_launches": args.steps,
+        "clocks": clocks,
+    }
+    if e2e is not None:
+        line["e2e"] = {"value": round(flops_total / (e2e_ms_max / 1e3) / 1e12, 2), "unit": UNIT,
+                       "h2d_bytes_per_step": e2e["h2d"], "d2h_bytes_per_step": e2e["d2h"],
+                       "ms_per_step": round(e2e_ms_max, 4),
+                       "path": "llm_fa_b200.attention_forward, pinned host buffers"}
+        line["gpu_launches"] += args.steps
+    if world == 1 and not args.no_cpu_baseline:
+        line["cpu_baseline"] = cpu_baseline(cfg, args.cpu_seconds)
+    return line
+
+
+# ------------------------------------------------------------------ reference arm
+def run_reference(args, cfg, world, rank, local):
+    if rank != 0:
+        return None
+    line = {"metric": METRIC, "unit": UNIT, "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "higher_is_better": True, "impl": "reference",
+            "dtype": "bf16", "data": "synthetic (seeded N(0,1) bf16 inputs, BASELINE.json shapes)",
+            "vs_baseline": None}
+    import torch
+    mod = None
+    try:
+        from oracle.build_ref import load_module
+        if torch.cuda.is_available():
+            mod = load_module()
+    except Exception as exc:  # fall back to the CPU oracle path
+        print(f"# reference kernel unavailable ({exc}); timing the CPU oracle path",
+              file=sys.stderr)
+    cpu = cpu_baseline(cfg, args.cpu_seconds)
+    if mod is None:
+        line.update({"value": round(cpu["value"], 6), "scaling": "weak",
+                     "ms_per_step": None, "cpu_baseline": cpu,
+                     "config": {"workload": f"{cfg.name}: {cfg.describe()}",
+                                "parallelism": "CPU, all host threads"},
+                     "e2e": {"value": round(cpu["value"], 6), "unit": UNIT,
+                             "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}})
+        return line
+    from torch.profiler import ProfilerActivity, profile
+
+    from llm_fa_b200.workloads import make_inputs
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    q, k, v = make_inputs(cfg)
+    # the reference takes 2-D (q,128)/(sk,128) contiguous tensors: one launch per (b, h)
+    heads = [(b, h) for b in range(cfg.batch) for h in range(cfg.heads)]
+    per_head = [(q[b, :, h].contiguous().to(dev), k[b, :, h].contiguous().to(dev),
+                 v[b, :, h].contiguous().to(dev)) for b, h in heads]
+    flush = torch.empty(L2_FLUSH_BYTES, dtype=torch.uint8, device=dev)
+    for _ in range(max(args.warmup, 3)):
+        for Q, K, V in per_head:
+            mod.llm_fa_forward(Q, K, V)
+    torch.cuda.synchronize()
+    with profile(activities=[ProfilerActivity.CUDA]) as prof:
+        for _ in range(args.steps):
+            flush.zero_()
+            for Q, K, V in per_head:
+                mod.llm_fa_forward(Q, K, V)
+        torch.cuda.synchronize()
+    durs = [e.device_time_total for e in prof.events()
+            if "llm_fa_kernel" in e.name and e.device_type == torch.autograd.DeviceType.CUDA]
+    total_us = sum(durs)
+    step_ms = total_us / 1e3 / args.steps
+    value = cfg.flops / (step_ms / 1e3) / 1e12
+    line.update({
+        "value": round(value, 2), "ms_per_step": round(step_ms, 5), "scaling": "weak",
+        "config": {"workload": f"{cfg.name}: {cfg.describe()} non-causal",
+                   "parallelism": "single GPU, one 2-D launch per (batch, head)",
+                   "l2": "flushed between timed steps (256 MiB write)",
+                   "timing": f"CUPTI kernel durations of {len(durs)} llm_fa_kernel launches"},
+        "kernel_us_per_launch": round(total_us / max(len(durs), 1), 2),
+        "gpu_launches": len(durs),
+        "cpu_baseline": cpu,
+        "e2e": {"value": round(value, 2), "unit": UNIT, "h2d_bytes_per_step": 0,
+                "d2h_bytes_per_step": 0},
+    })
+    return line
+
+
+def main():
+    args = parse_args()
+    world, rank, local = dist_env()
+    if world != args.gpus:
+        print(f"# note: --gpus {args.gpus} but WORLD_SIZE={world}; using WORLD_SIZE",
+              file=sys.stderr)
+    from llm_fa_b200.workloads import CONFIGS
+    cfg = CONFIGS[args.config]
+    if args.impl == "reference":
+        line = run_reference(args, cfg, world, rank, local)
+        if line is not None:
+            print(json.dumps(line), flush=True)
+        return
+    import torch.distributed as dist
+    if world > 1:
+        import torch
+        torch.cuda.set_device(local)
+        dist.init_process_group("nccl", timeout=timedelta(seconds=300),
+                                device_id=torch.device("cuda", local))
+    try:
+        line = run_ours(args, cfg, world, rank, local)
+    finally:
+        if world > 1:
+            dist.destroy_process_group()
+    if line is not None:
+        print(json.dumps(line), flush=True)
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,101 @@
+/*
+ * llm_fa_b200 — C ABI of the B200 (sm_100a) FlashAttention forward.
+ *
+ * Plain pointers and sizes only: no torch types cross this boundary. Every
+ * entry point returns an llmfa status code (0 = success) and never aborts the
+ * process. Compute entry points are asynchronous on the caller's stream and
+ * allocate nothing; the caller owns every buffer.
+ *
+ * The reference exposes its path through one pybind function,
+ *   std::vector<torch::Tensor> llm_fa_forward(Tensor Q, Tensor K, Tensor V)
+ *   (llm_fa.cu:1418-1475, bound in llm_fa.py:37-54),
+ * which checks shapes with TORCH_CHECK, encodes the TMA tensor maps, allocates
+ * O, launches `llm_fa_kernel` on the legacy default stream and synchronises
+ * the device. The functions below split that into an allocation-free launch
+ * on an explicit stream plus status queries.
+ */
+#ifndef LLM_FA_B200_H_
+#define LLM_FA_B200_H_
+
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* Status codes. */
+#define LLMFA_OK 0
+#define LLMFA_ERR_INVALID_ARGUMENT 1 /* null pointer, non-positive size, bad scale */
+#define LLMFA_ERR_UNSUPPORTED 2      /* alignment/stride outside what the TMA path accepts */
+#define LLMFA_ERR_TENSOR_MAP 3       /* cuTensorMapEncodeTiled rejected a descriptor */
+#define LLMFA_ERR_LAUNCH 4           /* kernel launch failed */
+#define LLMFA_ERR_CUDA 5             /* other CUDA runtime/driver failure (no device, ...) */
+#define LLMFA_ERR_DEVICE_TIMEOUT 6   /* a bounded in-kernel wait gave up (see llmfa_device_status) */
+
+/*
+ * O = softmax(Q K^T * softmax_scale) V for bf16 tensors with head dim 128,
+ * non-causal, fp32 softmax state, bf16 output.
+ *
+ * Replaces llm_fa_forward (llm_fa.cu:1418-1475) and generalises its 2-D
+ * (q,128)/(sk,128) inputs to the [B, S, H, 128] layout:
+ *   q: [batch, seq_q, heads, 128]   k, v: [batch, seq_k, heads, 128]
+ *   o: [batch, seq_q, heads, 128]   (written; may not alias q, k or v)
+ * Each *_strides array holds the element strides of the (batch, seq, head)
+ * dimensions; the head-dim stride must be 1. Base pointers must be 16-byte
+ * aligned and strides multiples of 8 elements (16 bytes). Any seq_q >= 1 and
+ * seq_k >= 1 are accepted (the reference requires q % 512 == 0,
+ * sk % 128 == 0, sk >= 256; llm_fa.cu:1421-1428).
+ * `stream` is a cudaStream_t (NULL = legacy default stream). No device
+ * synchronisation; no allocation.
+ */
+int llmfa_forward(const void* q, const int64_t q_strides[3], const void* k,
+                  const int64_t k_strides[3], const void* v, const int64_t v_strides[3], void* o,
+                  const int64_t o_strides[3], int64_t batch, int64_t heads, int64_t seq_q,
+                  int64_t seq_k, float softmax_scale, void* stream);
+
+/*
+ * The reference call shape exactly: contiguous row-major Q (seq_q,128),
+ * K/V (seq_k,128), O (seq_q,128) bf16, softmax_scale = 1/sqrt(128)
+ * (llm_fa.py:57-65, llm_fa.cu:1418-1475). Asynchronous; O must be allocated
+ * by the caller.
+ */
+int llmfa_forward_2d(const void* q, const void* k, const void* v, void* o, int64_t seq_q,
+                     int64_t seq_k, void* stream);
+
+/* Reads (and keeps) the device status word of the current device after
+ * synchronising `stream`: 0, or LLMFA_DEVICE_STATUS_TIMEOUT_BASE + wait-site
+ * id when an in-kernel wait gave up. No counterpart in the reference, whose
+ * waits are unbounded (llm_fa.cu:197-209). */
+#define LLMFA_DEVICE_STATUS_TIMEOUT_BASE 0x1000
+int llmfa_device_status(int* out_status, void* stream);
+/* Clears the device status word of the current device (stream-ordered). */
+int llmfa_reset_device_status(void* stream);
+
+/* Upper bound, in milliseconds, on every in-kernel wait (default 2000;
+ * environment variable LLMFA_WAIT_TIMEOUT_MS overrides the default). */
+int llmfa_set_wait_timeout_ms(uint32_t ms);
+
+/* Number of 2-CTA clusters of the attention kernel that can be resident at
+ * once on the current device (the persistent grid size). */
+int llmfa_max_active_clusters(int* out_clusters);
+
+/* Human-readable text for a status code. */
+const char* llmfa_error_string(int status);
+
+/* Library version (major*10000 + minor*100 + patch). */
+int llmfa_version(void);
+
+/*
+ * Failure-detection self test: launches one CTA whose single mbarrier wait can
+ * never complete (nothing arrives on it); the bounded wait gives up after
+ * `timeout_us` microseconds and records LLMFA_DEVICE_STATUS_TIMEOUT_BASE +
+ * 15 in the device status word. The GPU context stays usable. No counterpart
+ * in the reference.
+ */
+int llmfa_selftest_wait_timeout(uint32_t timeout_us, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* LLM_FA_B200_H_ */

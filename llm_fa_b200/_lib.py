@@ -1,0 +1,85 @@
+"""ctypes binding of the C ABI in include/llm_fa_b200.h.
+
+The shared library is the only compute path: if it is missing or cannot be
+loaded, every entry point raises instead of falling back to anything else.
+"""
+from __future__ import annotations
+
+import ctypes
+import os
+import threading
+from pathlib import Path
+
+LIB_PATH = Path(__file__).resolve().parent / "libllm_fa_b200.so"
+
+# status codes (include/llm_fa_b200.h)
+LLMFA_OK = 0
+LLMFA_ERR_INVALID_ARGUMENT = 1
+LLMFA_ERR_UNSUPPORTED = 2
+LLMFA_ERR_TENSOR_MAP = 3
+LLMFA_ERR_LAUNCH = 4
+LLMFA_ERR_CUDA = 5
+LLMFA_ERR_DEVICE_TIMEOUT = 6
+DEVICE_STATUS_TIMEOUT_BASE = 0x1000
+
+_I64x3 = ctypes.c_int64 * 3
+_lock = threading.Lock()
+_lib = None
+
+# name -> (restype, argtypes); every function declared in include/llm_fa_b200.h
+SIGNATURES = {
+    "llmfa_forward": (ctypes.c_int, [
+        ctypes.c_void_p, _I64x3, ctypes.c_void_p, _I64x3, ctypes.c_void_p, _I64x3,
+        ctypes.c_void_p, _I64x3, ctypes.c_int64, ctypes.c_int64, ctypes.c_int64,
+        ctypes.c_int64, ctypes.c_float, ctypes.c_void_p]),
+    "llmfa_forward_2d": (ctypes.c_int, [
+        ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p,
+        ctypes.c_int64, ctypes.c_int64, ctypes.c_void_p]),
+    "llmfa_device_status": (ctypes.c_int, [ctypes.POINTER(ctypes.c_int), ctypes.c_void_p]),
+    "llmfa_reset_device_status": (ctypes.c_int, [ctypes.c_void_p]),
+    "llmfa_set_wait_timeout_ms": (ctypes.c_int, [ctypes.c_uint32]),
+    "llmfa_max_active_clusters": (ctypes.c_int, [ctypes.POINTER(ctypes.c_int)]),
+    "llmfa_error_string": (ctypes.c_char_p, [ctypes.c_int]),
+    "llmfa_version": (ctypes.c_int, []),
+    "llmfa_selftest_wait_timeout": (ctypes.c_int, [ctypes.c_uint32, ctypes.c_void_p]),
+}
+
+
+class LlmfaError(RuntimeError):
+    """A nonzero llmfa status code."""
+
+    def __init__(self, code: int, what: str):
+        self.code = code
+        super().__init__(f"{what}: {error_string(code)} (status {code})")
+
+
+def lib() -> ctypes.CDLL:
+    """Load the shared library once; raise if it is not there."""
+    global _lib
+    if _lib is None:
+        with _lock:
+            if _lib is None:
+                if not LIB_PATH.exists():
+                    raise ImportError(
+                        f"{LIB_PATH.name} is not built; run `python -m llm_fa_b200.build` "
+                        "(there is no non-CUDA fallback)")
+                handle = ctypes.CDLL(str(LIB_PATH), mode=os.RTLD_NOW | os.RTLD_LOCAL)
+                for name, (res, args) in SIGNATURES.items():
+                    fn = getattr(handle, name)
+                    fn.restype = res
+                    fn.argtypes = args
+                _lib = handle
+    return _lib
+
+
+def error_string(code: int) -> str:
+    return lib().llmfa_error_string(int(code)).decode()
+
+
+def check(code: int, what: str) -> None:
+    if code != LLMFA_OK:
+        raise LlmfaError(code, what)
+
+
+def strides3(st) -> ctypes.Array:
+    return _I64x3(*[int(x) for x in st])

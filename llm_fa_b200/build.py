@@ -1,0 +1,71 @@
+"""Build the in-tree CUDA library `libllm_fa_b200.so` for sm_100a.
+
+One nvcc invocation, no torch dependency in the binary (static cudart); the
+driver entry point for tensor-map encoding is resolved at run time, so the
+library builds on a machine without a GPU and loads on a machine with one.
+
+    python -m llm_fa_b200.build [--force] [-v]
+"""
+from __future__ import annotations
+
+import argparse
+import os
+import shutil
+import subprocess
+import sys
+from pathlib import Path
+
+PKG = Path(__file__).resolve().parent
+CSRC = PKG / "csrc"
+INCLUDE = PKG.parent / "include"
+LIB = PKG / "libllm_fa_b200.so"
+SOURCES = [CSRC / "llm_fa_api.cu"]
+DEPS = SOURCES + sorted(CSRC.glob("*.cuh")) + sorted(INCLUDE.glob("*.h"))
+
+NVCC_FLAGS = [
+    "-gencode", "arch=compute_100a,code=sm_100a",
+    "-O3", "-lineinfo", "-std=c++17",
+    "-shared", "-Xcompiler", "-fPIC",
+    "-Xptxas", "-v",
+]
+
+
+def nvcc_path() -> str:
+    for cand in (os.environ.get("NVCC"), shutil.which("nvcc"), "/usr/local/cuda/bin/nvcc"):
+        if cand and Path(cand).exists():
+            return cand
+    raise RuntimeError("nvcc not found (set NVCC or put the CUDA toolkit on PATH)")
+
+
+def is_stale() -> bool:
+    if not LIB.exists():
+        return True
+    t = LIB.stat().st_mtime
+    return any(d.stat().st_mtime > t for d in DEPS)
+
+
+def build(force: bool = False, verbose: bool = False) -> Path:
+    """Compile the library if it is missing or older than its sources."""
+    if not force and not is_stale():
+        return LIB
+    tmp = LIB.with_suffix(".so.tmp")
+    cmd = [nvcc_path(), *NVCC_FLAGS, "-o", str(tmp), *map(str, SOURCES)]
+    proc = subprocess.run(cmd, capture_output=True, text=True)
+    if verbose or proc.returncode != 0:
+        sys.stderr.write(proc.stdout + proc.stderr)
+    if proc.returncode != 0:
+        raise RuntimeError(f"nvcc failed ({proc.returncode}): {' '.join(cmd)}")
+    # ptxas -v: the attention kernel must not spill
+    for line in (proc.stdout + proc.stderr).splitlines():
+        if "spill stores" in line and not line.strip().startswith("0 bytes stack frame, 0 bytes spill"):
+            sys.stderr.write(f"warning: register spills reported by ptxas: {line.strip()}\n")
+    os.replace(tmp, LIB)
+    return LIB
+
+
+if __name__ == "__main__":
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--force", action="store_true")
+    ap.add_argument("-v", "--verbose", action="store_true")
+    a = ap.parse_args()
+    print(build(force=a.force, verbose=a.verbose))

@@ -1,0 +1,682 @@
+// Warp-specialised FlashAttention forward for sm_100a (B200):
+// BF16 Q/K/V, head_dim 128, non-causal, BF16 O, FP32 softmax state.
+//
+// Replaces the reference kernel `llm_fa_kernel` (llm_fa.cu:589-1413) and keeps
+// its computation: O = softmax(Q K^T * scale) V with an online (streaming)
+// softmax over 128-key tiles, P rounded to bf16 before the PV product, lazy
+// rescaling of the O accumulator only when the running row maximum grows by
+// more than kRescaleThreshold (log2 units; the reference uses the same 8.0,
+// llm_fa.cu:857-866), and a final division by the row sum
+// (llm_fa.cu:1348-1406).
+//
+// Work unit: 512 query rows of one (batch, head), processed by a cluster of
+// two CTAs (a CTA pair). The pair issues tcgen05 MMAs with cta_group::2 and
+// M = 256: CTA rank r owns query rows [r*128, r*128+128) of each 256-row
+// "Q tile"; every CTA holds two Q tiles (tile 0, tile 1) that take turns on
+// the tensor core while the other tile's softmax runs.
+//
+//   S_t = Q_t K_j^T   (SS MMA 256x128x128; B = K_j, 64 keys from each CTA)
+//   P_t = exp2(S_t * scale*log2e - m_t)  (bf16, written over S_t in TMEM)
+//   O_t += P_t V_j    (TS MMA; A = P_t from TMEM, B = V_j, 64 dims per CTA)
+//
+// Tensor memory (512 columns x 128 lanes per CTA):
+//   S_0 [0,128)  S_1 [128,256)  O_0 [256,384)  O_1 [384,512); P_t = S_t[0,64).
+//
+// Warp roles (16 warps, 512 threads):
+//   0-3  softmax, tile 0          4-7  softmax, tile 1
+//   8-11 correction (O rescale) + epilogue (x 1/l, bf16, TMA store)
+//   12   MMA issue (leader CTA) + TMEM allocation
+//   13   TMA producer             14-15 idle
+//
+// The pair is persistent: cluster c processes units c, c + nclusters, ... in
+// (batch, head, query-block) order, so concurrently resident clusters share
+// K/V tiles in L2.
+//
+// No wait in this kernel is unbounded: every hand-off is an mbarrier, every
+// mbarrier wait gives up after `timeout_ns`, records the wait site in the
+// device status word, raises a CTA-wide abort flag, and every role then runs
+// to the common teardown (drain MMAs, cluster barrier, TMEM dealloc). No
+// cluster-multicast form of any instruction is used.
+#pragma once
+#include <cuda.h>
+
+#include <cstdint>
+
+#include "ptx.cuh"
+#include "softmax_exp2.cuh"
+
+namespace llmfa {
+
+constexpr int kHeadDim = 128;
+constexpr int kBlockM = 128;  // query rows per CTA per Q tile
+constexpr int kQTiles = 2;    // Q tiles per CTA (ping-pong)
+constexpr int kPair = 2;      // CTAs per cluster (cta_group::2)
+constexpr int kUnitRows = kBlockM * kPair * kQTiles;  // 512 query rows per unit
+constexpr int kBlockN = 128;  // keys per KV tile
+constexpr int kStages = 6;    // K/V ring stages (K and V alternate)
+constexpr int kThreads = 512;
+
+constexpr uint32_t kQTileBytes = kBlockM * kHeadDim * 2;            // 32 KB
+constexpr uint32_t kKVStageBytes = kBlockN * kHeadDim * 2 / kPair;  // 16 KB
+constexpr uint32_t kOStageBytes = kBlockM * kHeadDim * 2;           // 32 KB
+constexpr uint32_t kPanelBytes = kBlockM * 128;                     // 128 rows x 128 B
+
+constexpr uint32_t kSmemQ = 0;
+constexpr uint32_t kSmemKV = kSmemQ + kQTiles * kQTileBytes;    // 64 KB
+constexpr uint32_t kSmemO = kSmemKV + kStages * kKVStageBytes;  // 160 KB
+constexpr uint32_t kSmemBar = kSmemO + kOStageBytes;            // 192 KB
+
+// mbarrier indices (8 B each)
+constexpr int kBarQFull = 0;                        // [2] leader: both CTAs' Q tile landed
+constexpr int kBarQEmpty = kBarQFull + 2;           // [2] each: last QK of the unit done
+constexpr int kBarKVFull = kBarQEmpty + 2;          // [S] leader: both halves landed
+constexpr int kBarKVEmpty = kBarKVFull + kStages;   // [S] each: MMAs done reading the stage
+constexpr int kBarSFull = kBarKVEmpty + kStages;    // [2] each: S_t in TMEM
+constexpr int kBarPFull = kBarSFull + 2;            // [2] leader: P_t written, O_t corrected
+constexpr int kBarOFull = kBarPFull + 2;            // [2] each: last PV of the unit done
+constexpr int kBarStat = kBarOFull + 2;             // [2x4] softmax warp -> correction warp
+constexpr int kBarLsum = kBarStat + 8;              // [2x4] final row sums ready
+constexpr int kBarOStageFull = kBarLsum + 8;        // [1] 4 correction warps wrote staging
+constexpr int kBarOStageEmpty = kBarOStageFull + 1; // [1] TMA store finished reading staging
+constexpr int kBarDrain = kBarOStageEmpty + 1;      // [1] leader: teardown MMA drain
+constexpr int kNumBars = kBarDrain + 1;
+
+constexpr uint32_t kSmemScale = kSmemBar + 512;                 // float [2][128]
+constexpr uint32_t kSmemLsum = kSmemScale + kQTiles * kBlockM * 4;  // float [2][128]
+constexpr uint32_t kSmemTmemSlot = kSmemLsum + kQTiles * kBlockM * 4;
+constexpr uint32_t kSmemAbort = kSmemTmemSlot + 4;
+constexpr uint32_t kSmemUsed = kSmemAbort + 4;
+constexpr uint32_t kSmemBytes = kSmemUsed + 1024;  // + base-alignment slack
+static_assert(kNumBars * 8 <= 512, "barrier area");
+static_assert(kSmemBytes <= 227 * 1024, "shared memory budget");
+
+// setmaxnreg split of the 65536 registers (launch: 512 threads x 128):
+// 2 softmax warpgroups x 128 x 176 + correction 128 x 64 + control 128 x 96.
+constexpr uint32_t kRegsSoftmax = 176;
+constexpr uint32_t kRegsCorrection = 64;
+constexpr uint32_t kRegsControl = 96;
+static_assert(2 * 128 * kRegsSoftmax + 128 * kRegsCorrection + 128 * kRegsControl <= 65536,
+              "register split exceeds the launch allocation");
+
+constexpr float kRescaleThreshold = 8.0f;       // log2 units
+constexpr uint32_t kSoftmaxPolyMask = 0x8888u;  // pairs of each 32-column chunk on the FMA exp2
+
+// Device status word: 0 = ok; otherwise kStatusTimeoutBase + wait-site id.
+constexpr int kStatusTimeoutBase = 0x1000;
+enum WaitSite : int {
+  kSiteProdQEmpty = 1,
+  kSiteProdKVEmpty = 2,
+  kSiteMmaQFull = 3,
+  kSiteMmaKVFull = 4,
+  kSiteMmaPFull = 5,
+  kSiteSoftSFull = 6,
+  kSiteCorrStat = 7,
+  kSiteCorrLsum = 8,
+  kSiteEpiOFull = 9,
+  kSiteEpiStage = 10,
+  kSiteDrain = 11,
+};
+
+struct FwdParams {
+  int B, H, Sq, Sk;
+  int n_qblk;        // ceil(Sq / 512)
+  int n_kv;          // ceil(Sk / 128)
+  int n_units;       // B * H * n_qblk
+  int kv_tail;       // valid keys in the last KV tile (1..128)
+  float scale_log2;  // softmax_scale * log2(e)
+  unsigned long long timeout_ns;
+  int* status;       // device status word
+};
+
+struct WaitCtl {
+  volatile uint32_t* abort;
+  int* status;
+  unsigned long long timeout_ns;
+};
+
+// Slow path of a bounded wait. With honor_abort, returns early once another
+// role of this CTA has given up.
+__device__ __forceinline__ bool mbar_wait_slow(uint32_t bar, uint32_t parity, const WaitCtl& c,
+                                            int site, bool honor_abort) {
+  const uint64_t t0 = ptx::globaltimer_ns();
+  for (uint32_t it = 1;; ++it) {
+    if (ptx::mbar_try_wait(bar, parity)) return true;
+    if ((it & 63u) == 0) {
+      if (honor_abort && *c.abort) return false;
+      if (ptx::globaltimer_ns() - t0 > c.timeout_ns) {
+        *c.abort = 1u;
+        atomicCAS(c.status, 0, kStatusTimeoutBase + site);
+        return false;
+      }
+    }
+  }
+}
+__device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, const WaitCtl& c,
+                                          int site, bool honor_abort = true) {
+  if (ptx::mbar_try_wait(bar, parity)) return true;
+  return mbar_wait_slow(bar, parity, c, site, honor_abort);
+}
+
+// Bounded wait executed by all 32 lanes of a warp; the result is
+// warp-uniform so warp-collective instructions can follow it.
+__device__ __forceinline__ bool mbar_wait_warp(uint32_t bar, uint32_t parity, const WaitCtl& c,
+                                               int site) {
+  const bool ok = mbar_wait(bar, parity, c, site);
+  return __all_sync(0xffffffffu, ok);
+}
+
+struct UnitCoord {
+  int b, h, row0;
+};
+__device__ __forceinline__ UnitCoord decode_unit(const FwdParams& p, int u) {
+  const int bh = u / p.n_qblk;
+  const int qb = u - bh * p.n_qblk;
+  return {bh / p.H, bh % p.H, qb * kUnitRows};
+}
+
+// Maximum of 32 scores (raw bits) with independent 3-input max chains.
+__device__ __forceinline__ float chunk_max(const uint32_t (&r)[32]) {
+  float a0 = ptx::fmax3(__uint_as_float(r[0]), __uint_as_float(r[1]), __uint_as_float(r[2]));
+  float a1 = ptx::fmax3(__uint_as_float(r[3]), __uint_as_float(r[4]), __uint_as_float(r[5]));
+#pragma unroll
+  for (int k = 6; k < 30; k += 4) {
+    a0 = ptx::fmax3(a0, __uint_as_float(r[k + 0]), __uint_as_float(r[k + 1]));
+    a1 = ptx::fmax3(a1, __uint_as_float(r[k + 2]), __uint_as_float(r[k + 3]));
+  }
+  return ptx::fmax3(a0, a1, fmaxf(__uint_as_float(r[30]), __uint_as_float(r[31])));
+}
+
+// Scores of keys at or past the end of the sequence (last KV tile only) -> -inf.
+__device__ __forceinline__ void mask_tail(uint32_t (&r)[32], int col0, int kv_tail) {
+  if (kv_tail >= col0 + 32) return;
+#pragma unroll
+  for (int k = 0; k < 32; ++k)
+    if (col0 + k >= kv_tail) r[k] = __float_as_uint(-INFINITY);
+}
+
+// 32 scores -> 16 bf16x2 probabilities stored to TMEM at `t_p`; adds the fp32
+// probabilities to the running pair sum.
+__device__ __forceinline__ void exp_chunk(const uint32_t (&r)[32], uint64_t c2, uint64_t neg_m2,
+                                          uint64_t& lsum2, uint32_t t_p) {
+  uint32_t pk[16];
+#pragma unroll
+  for (int k = 0; k < 16; ++k) {
+    const uint64_t x2 = ptx::f2_fma(
+        ptx::f2_pack(__uint_as_float(r[2 * k]), __uint_as_float(r[2 * k + 1])), c2, neg_m2);
+    const uint64_t e2 = ((kSoftmaxPolyMask >> k) & 1u) ? exp2_poly_x2(x2) : exp2_mufu_x2(x2);
+    lsum2 = ptx::f2_add(lsum2, e2);
+    float e0, e1;
+    ptx::f2_unpack(e2, e0, e1);
+    pk[k] = ptx::bf16x2_pack(e0, e1);
+  }
+  ptx::tmem_st16(t_p, pk);
+}
+
+__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
+    llm_fa_kernel_sm100(const __grid_constant__ CUtensorMap tmQ,
+                        const __grid_constant__ CUtensorMap tmK,
+                        const __grid_constant__ CUtensorMap tmV,
+                        const __grid_constant__ CUtensorMap tmO, const FwdParams p) {
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  const uint32_t smem_base = (ptx::smem_u32(smem_raw) + 1023u) & ~1023u;
+  uint8_t* smem_gen = smem_raw + (smem_base - ptx::smem_u32(smem_raw));
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const uint32_t rank = ptx::cluster_ctarank();
+  const bool leader = (rank == 0);
+  const int cluster = static_cast<int>(ptx::cluster_id_x());
+  const int nclusters = static_cast<int>(ptx::ncluster_x());
+
+  auto bar = [&](int idx) -> uint32_t { return smem_base + kSmemBar + 8u * idx; };
+  float* sm_scale = reinterpret_cast<float*>(smem_gen + kSmemScale);
+  float* sm_lsum = reinterpret_cast<float*>(smem_gen + kSmemLsum);
+  volatile uint32_t* abort_flag = reinterpret_cast<volatile uint32_t*>(smem_gen + kSmemAbort);
+  const WaitCtl wc{abort_flag, p.status, p.timeout_ns};
+
+  // ------------------------------------------------------------ prologue
+  if (warp == 0 && lane == 0) {
+    for (int t = 0; t < 2; ++t) {
+      ptx::mbar_init(bar(kBarQFull + t), 1);
+      ptx::mbar_init(bar(kBarQEmpty + t), 1);
+      ptx::mbar_init(bar(kBarSFull + t), 1);
+      ptx::mbar_init(bar(kBarPFull + t), 16);  // 4 softmax + 4 correction warps x 2 CTAs
+      ptx::mbar_init(bar(kBarOFull + t), 1);
+    }
+    for (int s = 0; s < kStages; ++s) {
+      ptx::mbar_init(bar(kBarKVFull + s), 1);
+      ptx::mbar_init(bar(kBarKVEmpty + s), 1);
+    }
+    for (int k = 0; k < 8; ++k) {
+      ptx::mbar_init(bar(kBarStat + k), 1);
+      ptx::mbar_init(bar(kBarLsum + k), 1);
+    }
+    ptx::mbar_init(bar(kBarOStageFull), 4);
+    ptx::mbar_init(bar(kBarOStageEmpty), 1);
+    ptx::mbar_init(bar(kBarDrain), 1);
+    *abort_flag = 0u;
+    ptx::fence_mbar_init();
+  }
+  if (warp == 12) {
+    ptx::tmem_alloc<2>(smem_base + kSmemTmemSlot, 512);
+    ptx::tmem_relinquish<2>();
+  }
+  if (warp == 13 && lane == 0) {
+    ptx::prefetch_tmap(&tmQ);
+    ptx::prefetch_tmap(&tmK);
+    ptx::prefetch_tmap(&tmV);
+    ptx::prefetch_tmap(&tmO);
+  }
+  ptx::tc_fence_before();
+  __syncthreads();
+  ptx::cluster_sync();
+  ptx::tc_fence_after();
+  const uint32_t tmem_base = *reinterpret_cast<volatile uint32_t*>(smem_gen + kSmemTmemSlot);
+
+  const int n = p.n_kv;
+
+  if (warp < 8) {
+    // ========================================================== softmax
+    ptx::setmaxnreg_inc<kRegsSoftmax>();
+    const int tile = warp >> 2;
+    const int quarter = warp & 3;
+    const int row = quarter * 32 + lane;
+    const uint32_t t_s = tmem_base + (static_cast<uint32_t>(quarter * 32) << 16) + tile * 128;
+    const uint32_t pfull_leader = ptx::mapa(bar(kBarPFull + tile), 0);
+    const uint32_t stat_bar = bar(kBarStat + tile * 4 + quarter);
+    const uint32_t lsum_bar = bar(kBarLsum + tile * 4 + quarter);
+    const uint64_t c2 = ptx::f2_pack(p.scale_log2, p.scale_log2);
+    uint32_t s_phase = 0;
+    bool ok = true;
+    for (int u = cluster; u < p.n_units && ok; u += nclusters) {
+      float m = 0.f, l = 0.f;
+      for (int j = 0; j < n; ++j) {
+        if (!mbar_wait_warp(bar(kBarSFull + tile), s_phase, wc, kSiteSoftSFull)) {
+          ok = false;
+          break;
+        }
+        s_phase ^= 1u;
+        ptx::tc_fence_after();
+        // Pass 1: all 128 scores -> row max. Chunks 0-1 stay in registers;
+        // chunks 2-3 (columns 64-127, never overwritten by P) are re-read from
+        // TMEM in pass 2 behind the exponentials of chunks 0-1, which keeps
+        // the live set small enough for the softmax register budget.
+        uint32_t s0[32], s1[32];
+        float mt;
+        {
+          uint32_t s2[32], s3[32];
+          ptx::tmem_ld32(t_s + 0, s0);
+          ptx::tmem_ld32(t_s + 32, s1);
+          ptx::tmem_ld32(t_s + 64, s2);
+          ptx::tmem_ld32(t_s + 96, s3);
+          ptx::tmem_wait_ld();
+          if (j == n - 1) {
+            mask_tail(s0, 0, p.kv_tail);
+            mask_tail(s1, 32, p.kv_tail);
+            mask_tail(s2, 64, p.kv_tail);
+            mask_tail(s3, 96, p.kv_tail);
+          }
+          mt = fmaxf(fmaxf(chunk_max(s0), chunk_max(s1)), fmaxf(chunk_max(s2), chunk_max(s3))) *
+               p.scale_log2;
+        }
+        if (j == 0) {
+          m = mt;
+        } else {
+          float sc = 1.f;
+          if (mt > m + kRescaleThreshold) {
+            sc = ptx::ex2_mufu(m - mt);
+            m = mt;
+            l *= sc;
+          }
+          sm_scale[tile * kBlockM + row] = sc;
+          __syncwarp();
+          if (lane == 0) ptx::mbar_arrive(stat_bar);
+        }
+        // Pass 2: P = exp2(s * scale*log2e - m) -> bf16 -> TMEM columns [0, 64).
+        const uint64_t neg_m2 = ptx::f2_pack(-m, -m);
+        uint64_t lsum2 = ptx::f2_pack(0.f, 0.f);
+        {
+          uint32_t s2[32];
+          ptx::tmem_ld32(t_s + 64, s2);
+          exp_chunk(s0, c2, neg_m2, lsum2, t_s + 0);
+          uint32_t s3[32];
+          ptx::tmem_ld32(t_s + 96, s3);
+          exp_chunk(s1, c2, neg_m2, lsum2, t_s + 16);
+          ptx::tmem_wait_ld();
+          if (j == n - 1) {
+            mask_tail(s2, 64, p.kv_tail);
+            mask_tail(s3, 96, p.kv_tail);
+          }
+          exp_chunk(s2, c2, neg_m2, lsum2, t_s + 32);
+          exp_chunk(s3, c2, neg_m2, lsum2, t_s + 48);
+        }
+        float l0, l1;
+        ptx::f2_unpack(lsum2, l0, l1);
+        l += l0 + l1;
+        ptx::tmem_wait_st();
+        ptx::tc_fence_before();
+        __syncwarp();
+        if (lane == 0) ptx::mbar_arrive_cluster(pfull_leader);
+      }
+      if (!ok) break;
+      sm_lsum[tile * kBlockM + row] = l;
+      __syncwarp();
+      if (lane == 0) ptx::mbar_arrive(lsum_bar);
+    }
+    if (!ok) *abort_flag = 1u;
+    // every role returns to the launch register count before the shared teardown
+    ptx::setmaxnreg_dec<128>();
+  } else if (warp < 12) {
+    // ========================================================== correction + epilogue
+    ptx::setmaxnreg_dec<kRegsCorrection>();
+    const int quarter = warp - 8;
+    const int row = quarter * 32 + lane;
+    const uint32_t lane_off = static_cast<uint32_t>(quarter * 32) << 16;
+    const uint32_t sO = smem_base + kSmemO;
+    uint32_t stat_phase = 0;  // bit t: phase parity of the tile-t stat barrier
+    uint32_t lsum_phase = 0, o_phase = 0, stage_phase = 0;
+    bool ok = true;
+    bool first = true;
+    for (int u = cluster; u < p.n_units && ok; u += nclusters) {
+      const UnitCoord uc = decode_unit(p, u);
+      if (first) {
+        // j = 0 needs no correction: O_t is overwritten by the unit's first PV.
+        if (lane == 0) {
+          ptx::mbar_arrive_cluster(ptx::mapa(bar(kBarPFull + 0), 0));
+          ptx::mbar_arrive_cluster(ptx::mapa(bar(kBarPFull + 1), 0));
+        }
+        __syncwarp();
+        first = false;
+      }
+      for (int j = 1; j < n && ok; ++j) {
+#pragma unroll 1
+        for (int tile = 0; tile < 2; ++tile) {
+          if (!mbar_wait_warp(bar(kBarStat + tile * 4 + quarter), (stat_phase >> tile) & 1u, wc,
+                              kSiteCorrStat)) {
+            ok = false;
+            break;
+          }
+          stat_phase ^= 1u << tile;
+          const float sc = sm_scale[tile * kBlockM + row];
+          if (__any_sync(0xffffffffu, sc != 1.f)) {
+            // O_t is quiescent here: PV_t(j-1) completed before S_t(j) was
+            // signalled, and PV_t(j) waits for this warp's arrival below.
+            ptx::tc_fence_after();
+            const uint32_t t_o = tmem_base + lane_off + 256 + tile * 128;
+            const uint64_t sc2 = ptx::f2_pack(sc, sc);
+#pragma unroll 1
+            for (int c = 0; c < 4; ++c) {
+              uint32_t r[32];
+              ptx::tmem_ld32(t_o + 32 * c, r);
+              ptx::tmem_wait_ld();
+#pragma unroll
+              for (int k = 0; k < 32; k += 2) {
+                uint64_t v = ptx::f2_pack(__uint_as_float(r[k]), __uint_as_float(r[k + 1]));
+                v = ptx::f2_mul(v, sc2);
+                r[k] = static_cast<uint32_t>(v);
+                r[k + 1] = static_cast<uint32_t>(v >> 32);
+              }
+              ptx::tmem_st32(t_o + 32 * c, r);
+            }
+            ptx::tmem_wait_st();
+          }
+          ptx::tc_fence_before();
+          __syncwarp();
+          if (lane == 0) ptx::mbar_arrive_cluster(ptx::mapa(bar(kBarPFull + tile), 0));
+        }
+      }
+      if (!ok) break;
+      const bool has_next = (u + nclusters) < p.n_units;
+#pragma unroll 1
+      for (int tile = 0; tile < 2; ++tile) {
+        if (!mbar_wait_warp(bar(kBarLsum + tile * 4 + quarter), lsum_phase, wc, kSiteCorrLsum) ||
+            !mbar_wait_warp(bar(kBarOFull + tile), o_phase, wc, kSiteEpiOFull) ||
+            !mbar_wait_warp(bar(kBarOStageEmpty), stage_phase ^ 1u, wc, kSiteEpiStage)) {
+          ok = false;
+          break;
+        }
+        ptx::tc_fence_after();
+        const float inv_l = __frcp_rn(sm_lsum[tile * kBlockM + row]);
+        const uint32_t t_o = tmem_base + lane_off + 256 + tile * 128;
+#pragma unroll 1
+        for (int c = 0; c < 4; ++c) {
+          uint32_t r[32];
+          ptx::tmem_ld32(t_o + 32 * c, r);
+          ptx::tmem_wait_ld();
+          uint32_t pk[16];
+#pragma unroll
+          for (int k = 0; k < 16; ++k)
+            pk[k] = ptx::bf16x2_pack(__uint_as_float(r[2 * k]) * inv_l,
+                                     __uint_as_float(r[2 * k + 1]) * inv_l);
+          // 128-byte-swizzled staging, the layout the SWIZZLE_128B TMA store reads.
+          const uint32_t rowaddr = sO + (c >> 1) * kPanelBytes + row * 128;
+#pragma unroll
+          for (int q = 0; q < 4; ++q) {
+            const uint32_t chunk = static_cast<uint32_t>(((c & 1) * 4 + q) ^ (row & 7));
+            asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(rowaddr + chunk * 16),
+                         "r"(pk[4 * q]), "r"(pk[4 * q + 1]), "r"(pk[4 * q + 2]),
+                         "r"(pk[4 * q + 3])
+                         : "memory");
+          }
+        }
+        // O_t has been read: the next unit's first PV may overwrite it.
+        ptx::tc_fence_before();
+        ptx::fence_proxy_async_smem();
+        __syncwarp();
+        if (lane == 0) {
+          if (has_next) ptx::mbar_arrive_cluster(ptx::mapa(bar(kBarPFull + tile), 0));
+          ptx::mbar_arrive(bar(kBarOStageFull));
+        }
+        int stored = 1;
+        if (warp == 8 && lane == 0) {
+          stored = mbar_wait(bar(kBarOStageFull), stage_phase, wc, kSiteEpiStage) ? 1 : 0;
+          if (stored) {
+            const int orow = uc.row0 + tile * (kBlockM * kPair) + static_cast<int>(rank) * kBlockM;
+            ptx::tma_store_4d(&tmO, sO, 0, uc.h, orow, uc.b);
+            ptx::tma_store_4d(&tmO, sO + kPanelBytes, 64, uc.h, orow, uc.b);
+            ptx::bulk_commit_group();
+            ptx::bulk_wait_group_read0();
+            ptx::mbar_arrive(bar(kBarOStageEmpty));
+          }
+        }
+        stored = __shfl_sync(0xffffffffu, stored, 0);
+        stage_phase ^= 1u;
+        if (!stored) {
+          ok = false;
+          break;
+        }
+      }
+      lsum_phase ^= 1u;
+      o_phase ^= 1u;
+    }
+    if (!ok) *abort_flag = 1u;
+    if (warp == 8 && lane == 0) ptx::bulk_wait_group0();
+    __syncwarp();
+    ptx::setmaxnreg_inc<128>();
+  } else {
+    ptx::setmaxnreg_dec<kRegsControl>();
+    if (warp == 12 && leader && lane == 0) {
+      // ======================================================== MMA issue
+      const uint32_t idesc_qk = ptx::idesc_bf16_f32(kBlockM * kPair, kBlockN, false, false);
+      const uint32_t idesc_pv = ptx::idesc_bf16_f32(kBlockM * kPair, kHeadDim, false, true);
+      auto commit_both = [&](int b) {
+        ptx::mma_commit<2>(bar(b));
+        ptx::mma_commit<2>(ptx::mapa(bar(b), 1));
+      };
+      // Descriptors: the high half (SBO 1024 B, version, 128-byte swizzle) is
+      // shared; the low half advances by (byte offset >> 4) per K step.
+      const uint32_t dhi = ptx::smem_desc_sw128_hi(1024);
+      auto qk = [&](int tile, uint32_t stage) {
+        const uint32_t d = tmem_base + tile * 128;
+        const uint32_t alo = ptx::smem_desc_lo(smem_base + kSmemQ + tile * kQTileBytes, 16);
+        const uint32_t blo = ptx::smem_desc_lo(smem_base + kSmemKV + stage * kKVStageBytes, 16);
+#pragma unroll
+        for (int kk = 0; kk < 8; ++kk) {
+          const uint32_t aoff = ((kk >> 2) * kPanelBytes + (kk & 3) * 32) >> 4;
+          const uint32_t boff = ((kk >> 2) * (kKVStageBytes / 2) + (kk & 3) * 32) >> 4;
+          ptx::mma_ss<2>(d, ptx::make_desc(alo + aoff, dhi), ptx::make_desc(blo + boff, dhi),
+                         idesc_qk, kk > 0 ? 1u : 0u);
+        }
+      };
+      auto pv = [&](int tile, uint32_t stage, bool acc) {
+        const uint32_t d = tmem_base + 256 + tile * 128;
+        const uint32_t pa = tmem_base + tile * 128;
+        const uint32_t vlo =
+            ptx::smem_desc_lo(smem_base + kSmemKV + stage * kKVStageBytes, kKVStageBytes);
+#pragma unroll
+        for (int kk = 0; kk < 8; ++kk) {
+          ptx::mma_ts<2>(d, pa + kk * 8, ptx::make_desc(vlo + ((kk * 16 * 128) >> 4), dhi),
+                         idesc_pv, (acc || kk > 0) ? 1u : 0u);
+        }
+      };
+      auto kv_ready = [&](uint32_t t) -> bool {
+        return mbar_wait(bar(kBarKVFull + t % kStages), (t / kStages) & 1u, wc, kSiteMmaKVFull);
+      };
+      uint32_t kv_t = 0, q_use = 0;
+      uint32_t p_phase[2] = {0u, 0u};
+      bool ok = true;
+      for (int u = cluster; u < p.n_units && ok; u += nclusters) {
+        const uint32_t tb = kv_t;
+        const uint32_t sk0 = tb % kStages;
+        if (!mbar_wait(bar(kBarQFull + 0), q_use & 1u, wc, kSiteMmaQFull) || !kv_ready(tb)) {
+          ok = false;
+          break;
+        }
+        ptx::tc_fence_after();
+        qk(0, sk0);
+        commit_both(kBarSFull + 0);
+        if (!mbar_wait(bar(kBarQFull + 1), q_use & 1u, wc, kSiteMmaQFull)) {
+          ok = false;
+          break;
+        }
+        ptx::tc_fence_after();
+        qk(1, sk0);
+        commit_both(kBarSFull + 1);
+        commit_both(kBarKVEmpty + sk0);
+        if (n == 1) {
+          commit_both(kBarQEmpty + 0);
+          commit_both(kBarQEmpty + 1);
+        }
+        for (int j = 0; j < n; ++j) {
+          const uint32_t tv = tb + 2 * j + 1, tk = tb + 2 * j + 2;
+          const uint32_t sv = tv % kStages, sk = tk % kStages;
+          const bool more = (j + 1 < n);
+          if (!kv_ready(tv) || !mbar_wait(bar(kBarPFull + 0), p_phase[0], wc, kSiteMmaPFull)) {
+            ok = false;
+            break;
+          }
+          p_phase[0] ^= 1u;
+          ptx::tc_fence_after();
+          pv(0, sv, j > 0);
+          if (!more) commit_both(kBarOFull + 0);
+          if (more) {
+            if (!kv_ready(tk)) {
+              ok = false;
+              break;
+            }
+            ptx::tc_fence_after();
+            qk(0, sk);
+            commit_both(kBarSFull + 0);
+            if (j + 2 == n) commit_both(kBarQEmpty + 0);
+          }
+          if (!mbar_wait(bar(kBarPFull + 1), p_phase[1], wc, kSiteMmaPFull)) {
+            ok = false;
+            break;
+          }
+          p_phase[1] ^= 1u;
+          ptx::tc_fence_after();
+          pv(1, sv, j > 0);
+          commit_both(kBarKVEmpty + sv);
+          if (!more) commit_both(kBarOFull + 1);
+          if (more) {
+            qk(1, sk);
+            commit_both(kBarSFull + 1);
+            commit_both(kBarKVEmpty + sk);
+            if (j + 2 == n) commit_both(kBarQEmpty + 1);
+          }
+        }
+        kv_t = tb + 2 * n;
+        ++q_use;
+      }
+      if (!ok) *abort_flag = 1u;
+      // Drain: every MMA issued above completes before TMEM is released.
+      ptx::mma_commit<2>(bar(kBarDrain));
+      mbar_wait(bar(kBarDrain), 0, wc, kSiteDrain, /*honor_abort=*/false);
+    } else if (warp == 13 && lane == 0) {
+      // ======================================================== TMA producer
+      const uint64_t pol_q = ptx::policy_evict_first();
+      const uint64_t pol_kv = ptx::policy_evict_last();
+      uint32_t kv_t = 0, q_use = 0;
+      bool ok = true;
+      for (int u = cluster; u < p.n_units && ok; u += nclusters) {
+        const UnitCoord uc = decode_unit(p, u);
+        auto load_q = [&](int tile) -> bool {
+          if (!mbar_wait(bar(kBarQEmpty + tile), (q_use & 1u) ^ 1u, wc, kSiteProdQEmpty))
+            return false;
+          const uint32_t full = ptx::mapa(bar(kBarQFull + tile), 0);
+          if (leader) ptx::mbar_arrive_expect_tx(bar(kBarQFull + tile), kPair * kQTileBytes);
+          const int qrow = uc.row0 + tile * (kBlockM * kPair) + static_cast<int>(rank) * kBlockM;
+          const uint32_t dst = smem_base + kSmemQ + tile * kQTileBytes;
+          ptx::tma_load_4d<true>(dst, &tmQ, full, 0, uc.h, qrow, uc.b, pol_q);
+          ptx::tma_load_4d<true>(dst + kPanelBytes, &tmQ, full, 64, uc.h, qrow, uc.b, pol_q);
+          return true;
+        };
+        auto acquire = [&](uint32_t& stage, uint32_t& full) -> bool {
+          const uint32_t t = kv_t++;
+          stage = t % kStages;
+          if (!mbar_wait(bar(kBarKVEmpty + stage), ((t / kStages) & 1u) ^ 1u, wc,
+                         kSiteProdKVEmpty))
+            return false;
+          full = ptx::mapa(bar(kBarKVFull + stage), 0);
+          if (leader) ptx::mbar_arrive_expect_tx(bar(kBarKVFull + stage), kPair * kKVStageBytes);
+          return true;
+        };
+        auto load_k = [&](int j) -> bool {
+          uint32_t stage, full;
+          if (!acquire(stage, full)) return false;
+          const uint32_t dst = smem_base + kSmemKV + stage * kKVStageBytes;
+          const int krow = j * kBlockN + static_cast<int>(rank) * (kBlockN / kPair);
+          ptx::tma_load_4d<true>(dst, &tmK, full, 0, uc.h, krow, uc.b, pol_kv);
+          ptx::tma_load_4d<true>(dst + kKVStageBytes / 2, &tmK, full, 64, uc.h, krow, uc.b,
+                                 pol_kv);
+          return true;
+        };
+        auto load_v = [&](int j) -> bool {
+          uint32_t stage, full;
+          if (!acquire(stage, full)) return false;
+          const uint32_t dst = smem_base + kSmemKV + stage * kKVStageBytes;
+          ptx::tma_load_4d<true>(dst, &tmV, full, static_cast<int>(rank) * 64, uc.h,
+                                 j * kBlockN, uc.b, pol_kv);
+          return true;
+        };
+        ok = load_q(0) && load_k(0) && load_q(1);
+        for (int j = 0; j < n && ok; ++j) {
+          ok = load_v(j);
+          if (ok && j + 1 < n) ok = load_k(j + 1);
+        }
+        ++q_use;
+      }
+      if (!ok) {
+        *abort_flag = 1u;
+        // let copies already issued land before the CTA's shared memory is released
+        const uint64_t t0 = ptx::globaltimer_ns();
+        while (ptx::globaltimer_ns() - t0 < 20000ull) {
+        }
+      }
+    }
+    __syncwarp();
+    ptx::setmaxnreg_inc<128>();
+  }
+  __syncwarp();
+
+  // ------------------------------------------------------------ teardown
+  ptx::tc_fence_before();
+  __syncthreads();
+  ptx::cluster_sync();
+  if (warp == 12) {
+    ptx::tc_fence_after();
+    ptx::tmem_dealloc<2>(tmem_base, 512);
+  }
+}
+
+}  // namespace llmfa

@@ -1,0 +1,309 @@
+// Host side of the C ABI declared in include/llm_fa_b200.h: argument checks,
+// TMA tensor-map encoding, persistent-grid sizing and the launch of
+// llmfa::llm_fa_kernel_sm100 on the caller's stream.
+//
+// Mirrors the reference launcher llm_fa_forward (llm_fa.cu:1418-1475) with
+// three differences: (1) no allocation and no device synchronisation — O is
+// the caller's buffer and the launch is stream-ordered; (2) errors are status
+// codes instead of TORCH_CHECK exceptions; (3) [B, S, H, 128] strided views
+// instead of 2-D contiguous tensors, encoded as 4-D tensor maps (D, H, S, B)
+// so that out-of-range rows are zero-filled on load and clipped on store.
+#include <cuda.h>
+#include <cuda_runtime.h>
+#include <cudaTypedefs.h>
+
+#include <atomic>
+#include <cmath>
+#include <cstdint>
+#include <cstdlib>
+#include <mutex>
+
+#include "../../include/llm_fa_b200.h"
+#include "fa_fwd_kernel.cuh"
+
+namespace {
+
+constexpr int kVersion = 100;  // 0.1.0
+constexpr int kMaxDevices = 64;
+constexpr int kSiteSelftest = 15;
+
+__device__ int g_device_status = 0;
+
+struct DeviceSetup {
+  std::once_flag once;
+  int err = LLMFA_OK;
+  int* status_ptr = nullptr;  // device address of g_device_status on this device
+  int max_clusters = 0;
+};
+DeviceSetup g_setup[kMaxDevices];
+
+std::atomic<unsigned long long> g_timeout_ns{0};
+
+unsigned long long wait_timeout_ns() {
+  unsigned long long t = g_timeout_ns.load(std::memory_order_relaxed);
+  if (t == 0) {
+    unsigned long long ms = 2000;
+    if (const char* e = std::getenv("LLMFA_WAIT_TIMEOUT_MS")) {
+      const long long v = std::atoll(e);
+      if (v > 0) ms = static_cast<unsigned long long>(v);
+    }
+    t = ms * 1000000ull;
+    unsigned long long expected = 0;
+    g_timeout_ns.compare_exchange_strong(expected, t);
+    t = g_timeout_ns.load(std::memory_order_relaxed);
+  }
+  return t;
+}
+
+PFN_cuTensorMapEncodeTiled_v12000 get_encode_fn() {
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = [] {
+    void* ptr = nullptr;
+    cudaDriverEntryPointQueryResult q{};
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &ptr, cudaEnableDefault, &q) !=
+            cudaSuccess ||
+        q != cudaDriverEntryPointSuccess)
+      ptr = nullptr;
+    return reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(ptr);
+  }();
+  return fn;
+}
+
+// Once per device (with that device current): opt in to the kernel's shared
+// memory, look up the device address of the status word, size the grid.
+int device_setup(int* dev_out, DeviceSetup** out) {
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices) {
+    cudaGetLastError();
+    return LLMFA_ERR_CUDA;
+  }
+  DeviceSetup& s = g_setup[dev];
+  std::call_once(s.once, [&] {
+    if (cudaFuncSetAttribute(llmfa::llm_fa_kernel_sm100,
+                             cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             static_cast<int>(llmfa::kSmemBytes)) != cudaSuccess) {
+      cudaGetLastError();
+      s.err = LLMFA_ERR_CUDA;
+      return;
+    }
+    void* sp = nullptr;
+    if (cudaGetSymbolAddress(&sp, g_device_status) != cudaSuccess) {
+      cudaGetLastError();
+      s.err = LLMFA_ERR_CUDA;
+      return;
+    }
+    s.status_ptr = static_cast<int*>(sp);
+    int n = 0;
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(2, 1, 1);
+    cfg.blockDim = dim3(llmfa::kThreads, 1, 1);
+    cfg.dynamicSmemBytes = llmfa::kSmemBytes;
+    if (cudaOccupancyMaxActiveClusters(&n, llmfa::llm_fa_kernel_sm100, &cfg) != cudaSuccess ||
+        n <= 0) {
+      cudaGetLastError();
+      int sms = 0;
+      cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+      n = sms / 2;
+    }
+    s.max_clusters = n > 0 ? n : 1;
+  });
+  if (s.err != LLMFA_OK) return s.err;
+  *dev_out = dev;
+  *out = &s;
+  return LLMFA_OK;
+}
+
+bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+
+// Checks one [B, S, H, 128] view; returns a status code.
+int check_view(const void* ptr, const int64_t* st, int64_t seq, int64_t heads, int64_t batch) {
+  if (ptr == nullptr || st == nullptr) return LLMFA_ERR_INVALID_ARGUMENT;
+  if (!aligned16(ptr)) return LLMFA_ERR_UNSUPPORTED;
+  const int64_t dims[3] = {batch, seq, heads};
+  for (int i = 0; i < 3; ++i) {
+    if (dims[i] == 1) continue;  // stride of a size-1 dimension is never used
+    if (st[i] <= 0 || (st[i] % 8) != 0 || st[i] >= (int64_t(1) << 38))
+      return LLMFA_ERR_UNSUPPORTED;
+  }
+  return LLMFA_OK;
+}
+
+// 4-D map over (D=128, H, S, B) with a (64, 1, rows, 1) box and 128-byte swizzle.
+int encode_bshd(CUtensorMap* m, const void* ptr, const int64_t* st, int64_t seq, int64_t heads,
+                int64_t batch, uint32_t box_rows) {
+  PFN_cuTensorMapEncodeTiled_v12000 enc = get_encode_fn();
+  if (enc == nullptr) return LLMFA_ERR_CUDA;
+  // Size-1 dimensions get a canonical stride (their stride is never applied).
+  const uint64_t sh = heads == 1 ? 128 : static_cast<uint64_t>(st[2]);
+  const uint64_t ss = seq == 1 ? sh * static_cast<uint64_t>(heads) : static_cast<uint64_t>(st[1]);
+  const uint64_t sb = batch == 1 ? ss * static_cast<uint64_t>(seq) : static_cast<uint64_t>(st[0]);
+  cuuint64_t dims[4] = {128, static_cast<cuuint64_t>(heads), static_cast<cuuint64_t>(seq),
+                        static_cast<cuuint64_t>(batch)};
+  cuuint64_t strides[3] = {sh * 2, ss * 2, sb * 2};
+  cuuint32_t box[4] = {64, 1, box_rows, 1};
+  cuuint32_t estr[4] = {1, 1, 1, 1};
+  const CUresult r = enc(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 4, const_cast<void*>(ptr), dims,
+                         strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                         CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                         CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS ? LLMFA_OK : LLMFA_ERR_TENSOR_MAP;
+}
+
+__global__ void llmfa_wait_selftest_kernel(unsigned long long timeout_ns, int* status) {
+  __shared__ __align__(8) uint64_t bar;
+  __shared__ uint32_t abort_flag;
+  const uint32_t b = llmfa::ptx::smem_u32(&bar);
+  if (threadIdx.x == 0) {
+    llmfa::ptx::mbar_init(b, 1);
+    abort_flag = 0u;
+    llmfa::ptx::fence_mbar_init();
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    const llmfa::WaitCtl c{&abort_flag, status, timeout_ns};
+    // Nothing arrives on `bar`: phase 0 never completes and the wait gives up.
+    if (!llmfa::mbar_wait(b, 0, c, kSiteSelftest, false)) {
+      // the status word already holds the wait site
+    }
+  }
+}
+
+}  // namespace
+
+extern "C" {
+
+int llmfa_version(void) { return kVersion; }
+
+const char* llmfa_error_string(int status) {
+  switch (status) {
+    case LLMFA_OK: return "ok";
+    case LLMFA_ERR_INVALID_ARGUMENT: return "invalid argument";
+    case LLMFA_ERR_UNSUPPORTED: return "unsupported layout (alignment/stride)";
+    case LLMFA_ERR_TENSOR_MAP: return "tensor map encoding failed";
+    case LLMFA_ERR_LAUNCH: return "kernel launch failed";
+    case LLMFA_ERR_CUDA: return "CUDA runtime error";
+    case LLMFA_ERR_DEVICE_TIMEOUT: return "in-kernel wait timed out";
+    default: return "unknown status";
+  }
+}
+
+int llmfa_set_wait_timeout_ms(uint32_t ms) {
+  if (ms == 0) return LLMFA_ERR_INVALID_ARGUMENT;
+  g_timeout_ns.store(static_cast<unsigned long long>(ms) * 1000000ull);
+  return LLMFA_OK;
+}
+
+int llmfa_forward(const void* q, const int64_t q_strides[3], const void* k,
+                  const int64_t k_strides[3], const void* v, const int64_t v_strides[3], void* o,
+                  const int64_t o_strides[3], int64_t batch, int64_t heads, int64_t seq_q,
+                  int64_t seq_k, float softmax_scale, void* stream) {
+  // ---- argument checks (no CUDA call before they pass)
+  if (batch < 1 || heads < 1 || seq_q < 1 || seq_k < 1) return LLMFA_ERR_INVALID_ARGUMENT;
+  if (!(softmax_scale > 0.f) || !std::isfinite(softmax_scale)) return LLMFA_ERR_INVALID_ARGUMENT;
+  if (seq_q >= (int64_t(1) << 31) || seq_k >= (int64_t(1) << 31) || heads >= (1 << 24) ||
+      batch >= (1 << 24))
+    return LLMFA_ERR_UNSUPPORTED;
+  const int64_t n_qblk = (seq_q + llmfa::kUnitRows - 1) / llmfa::kUnitRows;
+  const int64_t n_units = batch * heads * n_qblk;
+  if (n_units >= (int64_t(1) << 31)) return LLMFA_ERR_UNSUPPORTED;
+  int rc;
+  if ((rc = check_view(q, q_strides, seq_q, heads, batch)) != LLMFA_OK) return rc;
+  if ((rc = check_view(k, k_strides, seq_k, heads, batch)) != LLMFA_OK) return rc;
+  if ((rc = check_view(v, v_strides, seq_k, heads, batch)) != LLMFA_OK) return rc;
+  if ((rc = check_view(o, o_strides, seq_q, heads, batch)) != LLMFA_OK) return rc;
+
+  int dev = 0;
+  DeviceSetup* s = nullptr;
+  if ((rc = device_setup(&dev, &s)) != LLMFA_OK) return rc;
+
+  CUtensorMap tq, tk, tv, to;
+  if ((rc = encode_bshd(&tq, q, q_strides, seq_q, heads, batch, llmfa::kBlockM)) != LLMFA_OK)
+    return rc;
+  if ((rc = encode_bshd(&tk, k, k_strides, seq_k, heads, batch, llmfa::kBlockN / llmfa::kPair)) !=
+      LLMFA_OK)
+    return rc;
+  if ((rc = encode_bshd(&tv, v, v_strides, seq_k, heads, batch, llmfa::kBlockN)) != LLMFA_OK)
+    return rc;
+  if ((rc = encode_bshd(&to, o, o_strides, seq_q, heads, batch, llmfa::kBlockM)) != LLMFA_OK)
+    return rc;
+
+  llmfa::FwdParams p{};
+  p.B = static_cast<int>(batch);
+  p.H = static_cast<int>(heads);
+  p.Sq = static_cast<int>(seq_q);
+  p.Sk = static_cast<int>(seq_k);
+  p.n_qblk = static_cast<int>(n_qblk);
+  p.n_kv = static_cast<int>((seq_k + llmfa::kBlockN - 1) / llmfa::kBlockN);
+  p.n_units = static_cast<int>(n_units);
+  p.kv_tail = static_cast<int>(seq_k - int64_t(p.n_kv - 1) * llmfa::kBlockN);
+  p.scale_log2 = softmax_scale * 1.4426950408889634f;
+  p.timeout_ns = wait_timeout_ns();
+  p.status = s->status_ptr;
+
+  const int nclusters = p.n_units < s->max_clusters ? p.n_units : s->max_clusters;
+  llmfa::llm_fa_kernel_sm100<<<dim3(2 * nclusters, 1, 1), dim3(llmfa::kThreads, 1, 1),
+                               llmfa::kSmemBytes, static_cast<cudaStream_t>(stream)>>>(tq, tk, tv,
+                                                                                       to, p);
+  if (cudaGetLastError() != cudaSuccess) return LLMFA_ERR_LAUNCH;
+  return LLMFA_OK;
+}
+
+int llmfa_forward_2d(const void* q, const void* k, const void* v, void* o, int64_t seq_q,
+                     int64_t seq_k, void* stream) {
+  const int64_t sq[3] = {seq_q * 128, 128, 128};
+  const int64_t sk[3] = {seq_k * 128, 128, 128};
+  return llmfa_forward(q, sq, k, sk, v, sk, o, sq, 1, 1, seq_q, seq_k,
+                       1.0f / std::sqrt(128.0f), stream);
+}
+
+int llmfa_device_status(int* out_status, void* stream) {
+  if (out_status == nullptr) return LLMFA_ERR_INVALID_ARGUMENT;
+  int dev = 0;
+  DeviceSetup* s = nullptr;
+  int rc = device_setup(&dev, &s);
+  if (rc != LLMFA_OK) return rc;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  if (cudaMemcpyAsync(out_status, s->status_ptr, sizeof(int), cudaMemcpyDeviceToHost, st) !=
+          cudaSuccess ||
+      cudaStreamSynchronize(st) != cudaSuccess) {
+    cudaGetLastError();
+    return LLMFA_ERR_CUDA;
+  }
+  return LLMFA_OK;
+}
+
+int llmfa_reset_device_status(void* stream) {
+  int dev = 0;
+  DeviceSetup* s = nullptr;
+  int rc = device_setup(&dev, &s);
+  if (rc != LLMFA_OK) return rc;
+  if (cudaMemsetAsync(s->status_ptr, 0, sizeof(int), static_cast<cudaStream_t>(stream)) !=
+      cudaSuccess) {
+    cudaGetLastError();
+    return LLMFA_ERR_CUDA;
+  }
+  return LLMFA_OK;
+}
+
+int llmfa_max_active_clusters(int* out_clusters) {
+  if (out_clusters == nullptr) return LLMFA_ERR_INVALID_ARGUMENT;
+  int dev = 0;
+  DeviceSetup* s = nullptr;
+  int rc = device_setup(&dev, &s);
+  if (rc != LLMFA_OK) return rc;
+  *out_clusters = s->max_clusters;
+  return LLMFA_OK;
+}
+
+int llmfa_selftest_wait_timeout(uint32_t timeout_us, void* stream) {
+  if (timeout_us == 0 || timeout_us > 10000000u) return LLMFA_ERR_INVALID_ARGUMENT;
+  int dev = 0;
+  DeviceSetup* s = nullptr;
+  int rc = device_setup(&dev, &s);
+  if (rc != LLMFA_OK) return rc;
+  llmfa_wait_selftest_kernel<<<1, 32, 0, static_cast<cudaStream_t>(stream)>>>(
+      static_cast<unsigned long long>(timeout_us) * 1000ull, s->status_ptr);
+  if (cudaGetLastError() != cudaSuccess) return LLMFA_ERR_LAUNCH;
+  return LLMFA_OK;
+}
+
+}  // extern "C"

@@ -1,0 +1,275 @@
+"""GPU parity tests of the sm_100a kernel through the C ABI.
+
+Reference semantics: fp32 SDPA on bf16-rounded inputs (validate.py:19-27);
+tolerance on O: max-abs 2e-2, mean-abs 2e-3. At the
+BASELINE sizes the CPU oracle checks a seeded subset of query rows (rows are
+independent), a chunked GPU fp32 SDPA checks every row, and size-independent
+properties (K/V permutation invariance, linearity in V, constant V) are
+checked on the full output.
+"""
+import math
+
+import numpy as np
+import pytest
+import torch
+import torch.nn.functional as F
+
+from llm_fa_b200 import _lib, attention_forward, device_status, reset_device_status
+from llm_fa_b200 import llm_fa as mirror
+from llm_fa_b200 import selftest_wait_timeout, set_wait_timeout_ms
+from llm_fa_b200.workloads import CONFIGS, Config, make_inputs, sample_rows
+from oracle.sdpa_oracle import MAX_ABS_TOL, MEAN_ABS_TOL, compare, sdpa_fp32
+
+pytestmark = pytest.mark.gpu
+
+
+@pytest.fixture(scope="module", autouse=True)
+def _cuda():
+    assert torch.cuda.is_available(), "GPU tests need a CUDA device"
+    major, minor = torch.cuda.get_device_capability()
+    assert (major, minor) == (10, 0), f"sm_100 required, found sm_{major}{minor}"
+    set_wait_timeout_ms(1000)
+    reset_device_status()
+    yield
+    torch.cuda.synchronize()
+
+
+def _run(q, k, v, scale=None):
+    o = attention_forward(q.cuda(), k.cuda(), v.cuda(), softmax_scale=scale)
+    torch.cuda.synchronize()
+    assert device_status() == 0
+    return o.cpu()
+
+
+def _assert_close(out, ref, max_tol=MAX_ABS_TOL, mean_tol=MEAN_ABS_TOL):
+    err = compare(out, ref)
+    assert err["nonfinite"] == 0, err
+    assert err["max_abs"] < max_tol and err["mean_abs"] < mean_tol, err
+    return err
+
+
+def _gpu_reference(q, k, v, scale, chunk=2048):
+    """fp32 SDPA on the GPU (TF32 off), chunked over query rows; [B,S,H,D] in, fp32 out."""
+    prev = torch.backends.cuda.matmul.allow_tf32
+    torch.backends.cuda.matmul.allow_tf32 = False
+    try:
+        B, Sq, H, D = q.shape
+        out = torch.empty(B, Sq, H, D, dtype=torch.float32, device=q.device)
+        kh = k.permute(0, 2, 1, 3).float()
+        vh = v.permute(0, 2, 1, 3).float()
+        with torch.nn.attention.sdpa_kernel(torch.nn.attention.SDPBackend.MATH):
+            for s0 in range(0, Sq, chunk):
+                qh = q[:, s0:s0 + chunk].permute(0, 2, 1, 3).float()
+                o = F.scaled_dot_product_attention(qh, kh, vh, scale=scale)
+                out[:, s0:s0 + chunk] = o.permute(0, 2, 1, 3)
+        return out
+    finally:
+        torch.backends.cuda.matmul.allow_tf32 = prev
+
+
+# ----------------------------------------------------------------- failure detection
+def test_bounded_wait_times_out_and_context_survives():
+    reset_device_status()
+    selftest_wait_timeout(2000)  # 2 ms; nothing ever arrives on the barrier
+    st = device_status()
+    assert st == _lib.DEVICE_STATUS_TIMEOUT_BASE + 15
+    reset_device_status()
+    assert device_status() == 0
+    q = torch.randn(512, 128, device="cuda").bfloat16()
+    o = attention_forward(q, q, q)
+    torch.cuda.synchronize()
+    assert torch.isfinite(o.float()).all()
+
+
+# ----------------------------------------------------------------- small shapes
+@pytest.mark.parametrize("Sq,Sk", [(512, 128), (512, 256), (1024, 1024), (512, 4096)])
+def test_single_head_aligned(Sq, Sk):
+    cfg = Config("t", 1, 1, Sq, Sk, seed=Sq + Sk)
+    q, k, v = make_inputs(cfg)
+    _assert_close(_run(q, k, v), sdpa_fp32(q, k, v))
+
+
+@pytest.mark.parametrize("Sq,Sk", [(1, 1), (7, 300), (128, 129), (300, 127), (511, 513),
+                                   (513, 1000), (1000, 77), (2000, 2049)])
+def test_ragged_lengths(Sq, Sk):
+    cfg = Config("r", 1, 2, Sq, Sk, seed=3 * Sq + Sk)
+    q, k, v = make_inputs(cfg)
+    _assert_close(_run(q, k, v), sdpa_fp32(q, k, v))
+
+
+def test_golden_cases_match():
+    g = np.load(__import__("pathlib").Path(__file__).with_name("golden") / "golden.npz")
+    for name in ("small", "ragged", "stress", "c1"):
+        B, H, Sq, Sk, seed, stress = (int(x) for x in g[f"{name}/config"])
+        cfg = Config(name, B, H, Sq, Sk, seed=seed, stress_rows=bool(stress))
+        q, k, v = make_inputs(cfg)
+        rows = torch.from_numpy(g[f"{name}/rows"])
+        o = _run(q, k, v)[:, rows]
+        _assert_close(o, torch.from_numpy(g[f"{name}/o"]))
+
+
+def test_baseline_config_c1_full():
+    cfg = CONFIGS["c1"]
+    q, k, v = make_inputs(cfg)
+    _assert_close(_run(q, k, v), sdpa_fp32(q, k, v))
+
+
+def test_known_answers():
+    g = torch.Generator().manual_seed(11)
+    q = torch.randn(1, 512, 1, 128, generator=g).bfloat16()
+    k = torch.randn(1, 640, 1, 128, generator=g).bfloat16()
+    # constant V -> O is that constant (up to bf16 rounding of P and O)
+    v = torch.full((1, 640, 1, 128), 0.625).bfloat16()
+    o = _run(q, k, v)
+    assert (o.float() - 0.625).abs().max().item() <= 4e-3
+    # identical keys -> uniform softmax -> mean(V)
+    kk = k[:, :1].expand(1, 640, 1, 128).contiguous()
+    v = torch.randn(1, 640, 1, 128, generator=g).bfloat16()
+    _assert_close(_run(q, kk, v), v.float().mean(dim=1, keepdim=True).expand_as(q.float()), 5e-3, 1e-3)
+    # one dominant key (logit gap ~ 90 in log2 units) -> that V row
+    kh = torch.zeros(1, 640, 1, 128).bfloat16()
+    kh[0, 333, 0] = 6.0
+    qh = torch.ones(1, 512, 1, 128).bfloat16()
+    o = _run(qh, kh, v)
+    _assert_close(o, v[:, 333:334].float().expand(1, 512, 1, 128), 1e-2, 1e-3)
+
+
+def test_softmax_scale_argument():
+    cfg = Config("s", 1, 1, 512, 512, seed=5)
+    q, k, v = make_inputs(cfg)
+    for scale in (0.02, 0.3):
+        _assert_close(_run(q, k, v, scale), sdpa_fp32(q, k, v, scale))
+
+
+def test_online_rescale_path_large_logits():
+    # rows whose max grows late in the sweep: later key tiles are larger
+    g = torch.Generator().manual_seed(21)
+    q = torch.randn(1, 512, 1, 128, generator=g).bfloat16()
+    k = torch.randn(1, 2048, 1, 128, generator=g)
+    k = (k * torch.linspace(0.2, 4.0, 2048).view(1, 2048, 1, 1)).bfloat16()
+    v = torch.randn(1, 2048, 1, 128, generator=g).bfloat16()
+    _assert_close(_run(q, k, v), sdpa_fp32(q, k, v))
+
+
+# ----------------------------------------------------------------- layouts
+def test_batched_multihead_persistent_units():
+    # 4*6*3 = 72 units of 512 rows: exercises the persistent loop
+    cfg = Config("bh", 4, 6, 1536, 700, seed=9)
+    q, k, v = make_inputs(cfg)
+    _assert_close(_run(q, k, v), sdpa_fp32(q, k, v))
+
+
+def test_many_units_more_than_resident_clusters():
+    cfg = Config("many", 2, 64, 1024, 256, seed=10)  # 256 units
+    q, k, v = make_inputs(cfg)
+    _assert_close(_run(q, k, v), sdpa_fp32(q, k, v))
+
+
+def test_strided_views_packed_qkv_and_out():
+    B, S, H = 2, 700, 3
+    g = torch.Generator().manual_seed(12)
+    qkv = torch.randn(B, S, 3, H, 128, generator=g).bfloat16().cuda()
+    q, k, v = qkv[:, :, 0], qkv[:, :, 1], qkv[:, :, 2]  # non-contiguous views
+    out_store = torch.zeros(B, S, H, 2 * 128, dtype=torch.bfloat16, device="cuda")
+    out = out_store[..., :128]  # strided output view
+    attention_forward(q, k, v, out=out)
+    torch.cuda.synchronize()
+    ref = sdpa_fp32(q.cpu(), k.cpu(), v.cpu())
+    _assert_close(out.cpu(), ref)
+    assert torch.count_nonzero(out_store[..., 128:]) == 0  # nothing written past the view
+
+
+def test_unaligned_pointer_is_rejected():
+    x = torch.randn(513 * 128 + 1, device="cuda").bfloat16()
+    q = x[1:].view(513, 128)  # 2-byte offset
+    with pytest.raises(RuntimeError, match="unsupported"):
+        attention_forward(q, q, q)
+
+
+def test_input_validation_errors():
+    q = torch.randn(512, 128, device="cuda").bfloat16()
+    with pytest.raises(RuntimeError, match="bfloat16"):
+        attention_forward(q.half(), q.half(), q.half())
+    with pytest.raises(RuntimeError, match="head dim"):
+        x = torch.randn(512, 64, device="cuda").bfloat16()
+        attention_forward(x, x, x)
+    with pytest.raises(RuntimeError, match="same shape"):
+        attention_forward(q, q, q[:100])
+
+
+def test_streams_and_determinism():
+    cfg = Config("d", 1, 4, 2048, 2048, seed=13)
+    q, k, v = (t.cuda() for t in make_inputs(cfg))
+    o1 = attention_forward(q, k, v)
+    s = torch.cuda.Stream()
+    with torch.cuda.stream(s):
+        o2 = attention_forward(q, k, v)
+    s.synchronize()
+    torch.cuda.synchronize()
+    assert torch.equal(o1, o2)
+
+
+# ----------------------------------------------------------------- reference surface
+def test_mirror_module_surface():
+    torch.manual_seed(0)
+    Q = torch.randn(1024, 128, device="cuda", dtype=torch.bfloat16)
+    K = torch.randn(2048, 128, device="cuda", dtype=torch.bfloat16)
+    V = torch.randn(2048, 128, device="cuda", dtype=torch.bfloat16)
+    res = mirror.mod.llm_fa_forward(Q, K, V)
+    assert isinstance(res, list) and len(res) == 3
+    O, prof_buf, prof_count = res
+    assert O.shape == (1024, 128) and O.dtype == torch.bfloat16
+    assert prof_buf.shape == (16384 * 6,) and prof_buf.dtype == torch.int32
+    assert prof_count.shape == (1,) and prof_count.dtype == torch.int32
+    ref = F.scaled_dot_product_attention(Q.view(1, 1, 1024, 128), K.view(1, 1, 2048, 128),
+                                         V.view(1, 1, 2048, 128), scale=1 / math.sqrt(128))
+    # validate.py's own PASS threshold against bf16 GPU SDPA (validate.py:41)
+    assert (O.float() - ref.view(1024, 128).float()).abs().max().item() < 5e-3
+    assert torch.equal(mirror.forward(Q, K, V), O)
+    out = mirror.run(q=512, sk=256, seed=0)
+    assert out[0].shape == (512, 128)
+
+
+# ----------------------------------------------------------------- BASELINE sizes
+def _sampled_parity(cfg, nrows, heads=None):
+    q, k, v = make_inputs(cfg)
+    o = attention_forward(q.cuda(), k.cuda(), v.cuda())
+    torch.cuda.synchronize()
+    assert device_status() == 0
+    rows = sample_rows(cfg, nrows)
+    hs = list(range(cfg.heads)) if heads is None else heads
+    for b in range(cfg.batch):
+        for h in hs:
+            ref = sdpa_fp32(q[b:b + 1, :, h:h + 1], k[b:b + 1, :, h:h + 1], v[b:b + 1, :, h:h + 1],
+                            rows=rows)
+            _assert_close(o[b:b + 1, rows, h:h + 1].cpu(), ref)
+    return q, k, v, o
+
+
+@pytest.mark.parametrize("name", ["c2", "c3"])
+def test_baseline_single_head_configs(name):
+    cfg = CONFIGS[name]
+    q, k, v, o = _sampled_parity(cfg, 256)
+    ref = _gpu_reference(q.cuda(), k.cuda(), v.cuda(), cfg.scale)
+    _assert_close(o, ref)
+
+
+def test_baseline_config_c4_sharded_heads():
+    cfg = CONFIGS["c4"]
+    q, k, v, o = _sampled_parity(cfg, 64, heads=[0, 17, 31])
+    ref = _gpu_reference(q.cuda(), k.cuda(), v.cuda(), cfg.scale)
+    _assert_close(o, ref)
+    # size-independent: permuting K and V rows together leaves O unchanged
+    perm = torch.randperm(cfg.seq_k, generator=torch.Generator().manual_seed(1))
+    o2 = attention_forward(q.cuda(), k[:, perm].cuda(), v[:, perm].cuda())
+    torch.cuda.synchronize()
+    _assert_close(o2, o.float(), 1e-2, 5e-4)
+
+
+def test_baseline_config_c5_softmax_stress():
+    cfg = CONFIGS["c5"]
+    q, k, v, o = _sampled_parity(cfg, 64, heads=[0, 21, 63])
+    # linearity in V on the full output: O(v) + O(-v) == 0 up to rounding
+    on = attention_forward(q.cuda(), k.cuda(), (-v).cuda())
+    torch.cuda.synchronize()
+    assert (o.float() + on.float()).abs().max().item() < 2e-2

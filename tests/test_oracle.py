@@ -1,0 +1,100 @@
+"""CPU tests: the oracle is pinned to the golden vectors, and the kernel's
+numerics (emulated on the CPU) stay within the parity tolerance."""
+from pathlib import Path
+
+import numpy as np
+import pytest
+import torch
+
+from llm_fa_b200.workloads import Config, make_inputs
+from oracle.sdpa_oracle import MAX_ABS_TOL, MEAN_ABS_TOL, attention_np, compare, sdpa_fp32
+from tests.kernel_emulation import attention_kernel_emulation, exp2_poly
+
+GOLDEN = Path(__file__).with_name("golden") / "golden.npz"
+CASES = ["small", "ragged", "stress", "c1"]
+
+
+@pytest.fixture(scope="module")
+def golden():
+    return np.load(GOLDEN)
+
+
+def _case(golden, name):
+    B, H, Sq, Sk, seed, stress = (int(x) for x in golden[f"{name}/config"])
+    cfg = Config(name, B, H, Sq, Sk, seed=seed, stress_rows=bool(stress))
+    rows = torch.from_numpy(golden[f"{name}/rows"])
+    return cfg, rows
+
+
+@pytest.mark.parametrize("name", CASES)
+def test_inputs_match_golden_generator(golden, name):
+    cfg, _ = _case(golden, name)
+    q, k, v = make_inputs(cfg)
+    got = np.array([t.float().double().sum().item() for t in (q, k, v)])
+    np.testing.assert_allclose(got, golden[f"{name}/input_checksum"], rtol=0, atol=1e-6)
+
+
+@pytest.mark.parametrize("name", CASES)
+def test_sdpa_oracle_matches_golden(golden, name):
+    cfg, rows = _case(golden, name)
+    q, k, v = make_inputs(cfg)
+    o = sdpa_fp32(q, k, v, cfg.scale, rows=rows)
+    np.testing.assert_allclose(o.numpy(), golden[f"{name}/o"], rtol=0, atol=2e-6)
+    full = sdpa_fp32(q, k, v, cfg.scale).double()
+    np.testing.assert_allclose(full.sum(dim=(1, 3)).numpy(), golden[f"{name}/o_sum"],
+                               rtol=1e-6, atol=1e-3)
+    np.testing.assert_allclose(full.abs().sum(dim=(1, 3)).numpy(), golden[f"{name}/o_abs_sum"],
+                               rtol=1e-6, atol=1e-3)
+
+
+@pytest.mark.parametrize("name", CASES)
+def test_numpy_restatement_matches_golden(golden, name):
+    cfg, rows = _case(golden, name)
+    q, k, v = make_inputs(cfg)
+    o = attention_np(q[:, rows].float().numpy(), k.float().numpy(), v.float().numpy(), cfg.scale)
+    # float64 restatement vs the fp32 golden: fp32 rounding of logits up to ~100
+    np.testing.assert_allclose(o, golden[f"{name}/o"], rtol=0, atol=2e-5)
+
+
+def test_known_answers_oracle():
+    g = torch.Generator().manual_seed(7)
+    q = torch.randn(1, 64, 1, 128, generator=g).bfloat16()
+    k = torch.randn(1, 200, 1, 128, generator=g).bfloat16()
+    # constant V rows -> O equals that row
+    v = torch.ones(1, 200, 1, 128).bfloat16() * 0.75
+    assert torch.allclose(sdpa_fp32(q, k, v), torch.full((1, 64, 1, 128), 0.75), atol=1e-6)
+    # identical keys -> uniform softmax -> O = mean(V)
+    k_same = k[:, :1].expand(1, 200, 1, 128).contiguous()
+    v = torch.randn(1, 200, 1, 128, generator=g).bfloat16()
+    expect = v.float().mean(dim=1, keepdim=True).expand(1, 64, 1, 128)
+    assert torch.allclose(sdpa_fp32(q, k_same, v), expect, atol=1e-5)
+    # one dominant key -> O = that value row
+    k_hot = torch.zeros(1, 200, 1, 128).bfloat16()
+    k_hot[0, 37, 0, :] = 8.0
+    q_hot = torch.ones(1, 64, 1, 128).bfloat16()
+    o = sdpa_fp32(q_hot, k_hot, v)
+    assert torch.allclose(o, v[:, 37:38].float().expand(1, 64, 1, 128), atol=1e-6)
+
+
+def test_exp2_polynomial_error_bound():
+    x = np.linspace(-125.0, 8.0, 2_000_001, dtype=np.float32)
+    got = exp2_poly(x).astype(np.float64)
+    ref = np.exp2(x.astype(np.float64))
+    rel = np.abs(got / ref - 1.0)
+    assert rel.max() < 1.0e-4  # Remez fit: 7.5e-5 in float32 Horner
+    assert np.all(exp2_poly(np.array([-1e30, -np.inf], np.float32)) < 1e-37)
+
+
+@pytest.mark.parametrize("name", ["small", "ragged", "stress"])
+def test_kernel_algorithm_emulation_within_tolerance(golden, name):
+    cfg, rows = _case(golden, name)
+    q, k, v = make_inputs(cfg)
+    ref = torch.from_numpy(golden[f"{name}/o"])
+    out = torch.empty_like(ref)
+    for b in range(cfg.batch):
+        for h in range(cfg.heads):
+            o = attention_kernel_emulation(q[b, :, h].float().numpy(), k[b, :, h].float().numpy(),
+                                           v[b, :, h].float().numpy(), cfg.scale)
+            out[b, :, h] = torch.from_numpy(o[rows.numpy()])
+    err = compare(out, ref)
+    assert err["max_abs"] < MAX_ABS_TOL and err["mean_abs"] < MEAN_ABS_TOL, err
