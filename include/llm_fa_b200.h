@@ -86,6 +86,16 @@ const char* llmfa_error_string(int status);
 int llmfa_version(void);
 
 /*
+ * Event trace of the last launch (library built with -DLLMFA_TRACE=1 only;
+ * otherwise returns LLMFA_ERR_UNSUPPORTED): copies the trace records
+ * ({uint64 globaltimer_ns, int64 clock64} per [cta rank][event][iteration])
+ * to host memory after synchronising the device. Replaces the reference's
+ * profiler ring flush (profiler.cuh:85-108) and the prof_buf / prof_count
+ * outputs of llm_fa_forward (llm_fa.cu:1461-1474).
+ */
+int llmfa_trace_read(void* dst_host, uint64_t capacity_bytes, uint64_t* written_bytes);
+
+/*
  * Failure-detection self test: launches one CTA whose single mbarrier wait can
  * never complete (nothing arrives on it); the bounded wait gives up after
  * `timeout_us` microseconds and records LLMFA_DEVICE_STATUS_TIMEOUT_BASE +

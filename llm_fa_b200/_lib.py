@@ -42,6 +42,8 @@ SIGNATURES = {
     "llmfa_error_string": (ctypes.c_char_p, [ctypes.c_int]),
     "llmfa_version": (ctypes.c_int, []),
     "llmfa_selftest_wait_timeout": (ctypes.c_int, [ctypes.c_uint32, ctypes.c_void_p]),
+    "llmfa_trace_read": (ctypes.c_int, [ctypes.c_void_p, ctypes.c_uint64,
+                                        ctypes.POINTER(ctypes.c_uint64)]),
 }
 
 

@@ -72,7 +72,8 @@ constexpr int kBarQEmpty = kBarQFull + 2;           // [2] each: last QK of the 
 constexpr int kBarKVFull = kBarQEmpty + 2;          // [S] leader: both halves landed
 constexpr int kBarKVEmpty = kBarKVFull + kStages;   // [S] each: MMAs done reading the stage
 constexpr int kBarSFull = kBarKVEmpty + kStages;    // [2] each: S_t in TMEM
-constexpr int kBarPFull = kBarSFull + 2;            // [2] leader: P_t written, O_t corrected
+constexpr int kBarPHalf = kBarSFull + 2;            // [2] leader: P_t keys 0-63 written, O_t corrected
+constexpr int kBarPFull = kBarPHalf + 2;            // [2] leader: P_t keys 64-127 written
 constexpr int kBarOFull = kBarPFull + 2;            // [2] each: last PV of the unit done
 constexpr int kBarStat = kBarOFull + 2;             // [2x4] softmax warp -> correction warp
 constexpr int kBarLsum = kBarStat + 8;              // [2x4] final row sums ready
@@ -98,8 +99,13 @@ constexpr uint32_t kRegsControl = 96;
 static_assert(2 * 128 * kRegsSoftmax + 128 * kRegsCorrection + 128 * kRegsControl <= 65536,
               "register split exceeds the launch allocation");
 
-constexpr float kRescaleThreshold = 8.0f;       // log2 units
-constexpr uint32_t kSoftmaxPolyMask = 0x8888u;  // pairs of each 32-column chunk on the FMA exp2
+constexpr float kRescaleThreshold = 8.0f;  // log2 units
+// Pairs (bit k = columns 2k, 2k+1) of each 32-column chunk whose exp2 runs on
+// the FMA pipe (softmax_exp2.cuh) instead of MUFU; the rest use ex2.approx.
+#ifndef LLMFA_SOFTMAX_POLY_MASK
+#define LLMFA_SOFTMAX_POLY_MASK 0x8888u
+#endif
+constexpr uint32_t kSoftmaxPolyMask = LLMFA_SOFTMAX_POLY_MASK;
 
 // Device status word: 0 = ok; otherwise kStatusTimeoutBase + wait-site id.
 constexpr int kStatusTimeoutBase = 0x1000;
@@ -116,6 +122,49 @@ enum WaitSite : int {
   kSiteEpiStage = 10,
   kSiteDrain = 11,
 };
+
+// ---------------------------------------------------------------- event trace
+// Intra-kernel event trace, compiled out unless LLMFA_TRACE=1. Cluster 0
+// records, for KV iterations [kTraceFirst, kTraceFirst + kTraceIters) of its
+// first unit and Q tile 0, the %globaltimer (ns) and %clock64 of each hand-off
+// below in both CTAs of the pair. Layout: [cta rank][event][iteration].
+#ifndef LLMFA_TRACE
+#define LLMFA_TRACE 0
+#endif
+constexpr int kTraceFirst = 32;
+constexpr int kTraceIters = 16;
+enum TraceEvent : int {
+  kEvSReady = 0,     // softmax: S_0(j) visible (after the s_full wait)
+  kEvLdDone,         // softmax: 128 scores in registers
+  kEvStat,           // softmax: rescale factor published
+  kEvPHalf,          // softmax: P keys 0-63 published
+  kEvPFull,          // softmax: P keys 64-127 published
+  kEvMmaPHalf,       // MMA: saw P half (about to issue PV k-steps 0-3)
+  kEvMmaPFull,       // MMA: saw P full (about to issue PV k-steps 4-7)
+  kEvMmaQK,          // MMA: QK_0(j+1) issued and committed
+  kEvCorrStat,       // correction: saw the rescale factor
+  kEvCorrArrive,     // correction: arrived on P half
+  kNumTraceEvents
+};
+struct TraceRecord {
+  unsigned long long globaltimer_ns;
+  long long clock;
+};
+constexpr int kTraceRecords = 2 * kNumTraceEvents * kTraceIters;
+#if LLMFA_TRACE
+__device__ TraceRecord g_trace[kTraceRecords];
+__device__ __forceinline__ void trace_event(int ev, int j, uint32_t rank, int cluster, int u) {
+  if (cluster == 0 && u == 0 && j >= kTraceFirst && j < kTraceFirst + kTraceIters) {
+    long long c;
+    asm volatile("mov.u64 %0, %%clock64;" : "=l"(c));
+    g_trace[(rank * kNumTraceEvents + ev) * kTraceIters + (j - kTraceFirst)] =
+        TraceRecord{ptx::globaltimer_ns(), c};
+  }
+}
+#define LLMFA_TRACE_EVENT(ev, j) trace_event((ev), (j), rank, cluster, u)
+#else
+#define LLMFA_TRACE_EVENT(ev, j) ((void)0)
+#endif
 
 struct FwdParams {
   int B, H, Sq, Sk;
@@ -240,7 +289,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
       ptx::mbar_init(bar(kBarQFull + t), 1);
       ptx::mbar_init(bar(kBarQEmpty + t), 1);
       ptx::mbar_init(bar(kBarSFull + t), 1);
-      ptx::mbar_init(bar(kBarPFull + t), 16);  // 4 softmax + 4 correction warps x 2 CTAs
+      ptx::mbar_init(bar(kBarPHalf + t), 16);  // 4 softmax + 4 correction warps x 2 CTAs
+      ptx::mbar_init(bar(kBarPFull + t), 8);   // 4 softmax warps x 2 CTAs
       ptx::mbar_init(bar(kBarOFull + t), 1);
     }
     for (int s = 0; s < kStages; ++s) {
@@ -282,6 +332,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
     const int quarter = warp & 3;
     const int row = quarter * 32 + lane;
     const uint32_t t_s = tmem_base + (static_cast<uint32_t>(quarter * 32) << 16) + tile * 128;
+    const uint32_t phalf_leader = ptx::mapa(bar(kBarPHalf + tile), 0);
     const uint32_t pfull_leader = ptx::mapa(bar(kBarPFull + tile), 0);
     const uint32_t stat_bar = bar(kBarStat + tile * 4 + quarter);
     const uint32_t lsum_bar = bar(kBarLsum + tile * 4 + quarter);
@@ -296,6 +347,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
           break;
         }
         s_phase ^= 1u;
+        if (warp == 0 && lane == 0) LLMFA_TRACE_EVENT(kEvSReady, j);
         ptx::tc_fence_after();
         // Pass 1: all 128 scores -> row max. Chunks 0-1 stay in registers;
         // chunks 2-3 (columns 64-127, never overwritten by P) are re-read from
@@ -310,6 +362,11 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
           ptx::tmem_ld32(t_s + 64, s2);
           ptx::tmem_ld32(t_s + 96, s3);
           ptx::tmem_wait_ld();
+          ptx::reg_fence32(s0);
+          ptx::reg_fence32(s1);
+          ptx::reg_fence32(s2);
+          ptx::reg_fence32(s3);
+          if (warp == 0 && lane == 0) LLMFA_TRACE_EVENT(kEvLdDone, j);
           if (j == n - 1) {
             mask_tail(s0, 0, p.kv_tail);
             mask_tail(s1, 32, p.kv_tail);
@@ -331,32 +388,43 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
           sm_scale[tile * kBlockM + row] = sc;
           __syncwarp();
           if (lane == 0) ptx::mbar_arrive(stat_bar);
+          if (warp == 0 && lane == 0) LLMFA_TRACE_EVENT(kEvStat, j);
         }
-        // Pass 2: P = exp2(s * scale*log2e - m) -> bf16 -> TMEM columns [0, 64).
+        // Pass 2: P = exp2(s * scale*log2e - m) -> bf16 -> TMEM columns [0, 64),
+        // published in two halves so the first four PV k-steps (keys 0-63)
+        // overlap the exponentials of keys 64-127.
         const uint64_t neg_m2 = ptx::f2_pack(-m, -m);
-        uint64_t lsum2 = ptx::f2_pack(0.f, 0.f);
+        uint64_t lsum_a = ptx::f2_pack(0.f, 0.f), lsum_b = lsum_a;
         {
           uint32_t s2[32];
           ptx::tmem_ld32(t_s + 64, s2);
-          exp_chunk(s0, c2, neg_m2, lsum2, t_s + 0);
+          exp_chunk(s0, c2, neg_m2, lsum_a, t_s + 0);
           uint32_t s3[32];
           ptx::tmem_ld32(t_s + 96, s3);
-          exp_chunk(s1, c2, neg_m2, lsum2, t_s + 16);
+          exp_chunk(s1, c2, neg_m2, lsum_b, t_s + 16);
+          ptx::tmem_wait_st();
+          ptx::tc_fence_before();
+          __syncwarp();
+          if (lane == 0) ptx::mbar_arrive_cluster(phalf_leader);
+          if (warp == 0 && lane == 0) LLMFA_TRACE_EVENT(kEvPHalf, j);
           ptx::tmem_wait_ld();
+          ptx::reg_fence32(s2);
+          ptx::reg_fence32(s3);
           if (j == n - 1) {
             mask_tail(s2, 64, p.kv_tail);
             mask_tail(s3, 96, p.kv_tail);
           }
-          exp_chunk(s2, c2, neg_m2, lsum2, t_s + 32);
-          exp_chunk(s3, c2, neg_m2, lsum2, t_s + 48);
+          exp_chunk(s2, c2, neg_m2, lsum_a, t_s + 32);
+          exp_chunk(s3, c2, neg_m2, lsum_b, t_s + 48);
         }
         float l0, l1;
-        ptx::f2_unpack(lsum2, l0, l1);
+        ptx::f2_unpack(ptx::f2_add(lsum_a, lsum_b), l0, l1);
         l += l0 + l1;
         ptx::tmem_wait_st();
         ptx::tc_fence_before();
         __syncwarp();
         if (lane == 0) ptx::mbar_arrive_cluster(pfull_leader);
+        if (warp == 0 && lane == 0) LLMFA_TRACE_EVENT(kEvPFull, j);
       }
       if (!ok) break;
       sm_lsum[tile * kBlockM + row] = l;
@@ -382,8 +450,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
       if (first) {
         // j = 0 needs no correction: O_t is overwritten by the unit's first PV.
         if (lane == 0) {
-          ptx::mbar_arrive_cluster(ptx::mapa(bar(kBarPFull + 0), 0));
-          ptx::mbar_arrive_cluster(ptx::mapa(bar(kBarPFull + 1), 0));
+          ptx::mbar_arrive_cluster(ptx::mapa(bar(kBarPHalf + 0), 0));
+          ptx::mbar_arrive_cluster(ptx::mapa(bar(kBarPHalf + 1), 0));
         }
         __syncwarp();
         first = false;
@@ -397,6 +465,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
             break;
           }
           stat_phase ^= 1u << tile;
+          if (warp == 8 && lane == 0 && tile == 0) LLMFA_TRACE_EVENT(kEvCorrStat, j);
           const float sc = sm_scale[tile * kBlockM + row];
           if (__any_sync(0xffffffffu, sc != 1.f)) {
             // O_t is quiescent here: PV_t(j-1) completed before S_t(j) was
@@ -409,6 +478,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
               uint32_t r[32];
               ptx::tmem_ld32(t_o + 32 * c, r);
               ptx::tmem_wait_ld();
+              ptx::reg_fence32(r);
 #pragma unroll
               for (int k = 0; k < 32; k += 2) {
                 uint64_t v = ptx::f2_pack(__uint_as_float(r[k]), __uint_as_float(r[k + 1]));
@@ -422,7 +492,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
           }
           ptx::tc_fence_before();
           __syncwarp();
-          if (lane == 0) ptx::mbar_arrive_cluster(ptx::mapa(bar(kBarPFull + tile), 0));
+          if (lane == 0) ptx::mbar_arrive_cluster(ptx::mapa(bar(kBarPHalf + tile), 0));
+          if (warp == 8 && lane == 0 && tile == 0) LLMFA_TRACE_EVENT(kEvCorrArrive, j);
         }
       }
       if (!ok) break;
@@ -443,6 +514,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
           uint32_t r[32];
           ptx::tmem_ld32(t_o + 32 * c, r);
           ptx::tmem_wait_ld();
+          ptx::reg_fence32(r);
           uint32_t pk[16];
 #pragma unroll
           for (int k = 0; k < 16; ++k)
@@ -464,7 +536,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
         ptx::fence_proxy_async_smem();
         __syncwarp();
         if (lane == 0) {
-          if (has_next) ptx::mbar_arrive_cluster(ptx::mapa(bar(kBarPFull + tile), 0));
+          if (has_next) ptx::mbar_arrive_cluster(ptx::mapa(bar(kBarPHalf + tile), 0));
           ptx::mbar_arrive(bar(kBarOStageFull));
         }
         int stored = 1;
@@ -518,13 +590,14 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
                          idesc_qk, kk > 0 ? 1u : 0u);
         }
       };
-      auto pv = [&](int tile, uint32_t stage, bool acc) {
+      // PV k-steps [k0, k0+4): keys 16*k0 .. 16*k0+63 of the tile.
+      auto pv_half = [&](int tile, uint32_t stage, bool acc, int k0) {
         const uint32_t d = tmem_base + 256 + tile * 128;
         const uint32_t pa = tmem_base + tile * 128;
         const uint32_t vlo =
             ptx::smem_desc_lo(smem_base + kSmemKV + stage * kKVStageBytes, kKVStageBytes);
 #pragma unroll
-        for (int kk = 0; kk < 8; ++kk) {
+        for (int kk = k0; kk < k0 + 4; ++kk) {
           ptx::mma_ts<2>(d, pa + kk * 8, ptx::make_desc(vlo + ((kk * 16 * 128) >> 4), dhi),
                          idesc_pv, (acc || kk > 0) ? 1u : 0u);
         }
@@ -533,7 +606,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
         return mbar_wait(bar(kBarKVFull + t % kStages), (t / kStages) & 1u, wc, kSiteMmaKVFull);
       };
       uint32_t kv_t = 0, q_use = 0;
-      uint32_t p_phase[2] = {0u, 0u};
+      uint32_t p_phase = 0;  // bit t: phase parity of tile t's P barriers
       bool ok = true;
       for (int u = cluster; u < p.n_units && ok; u += nclusters) {
         const uint32_t tb = kv_t;
@@ -561,13 +634,21 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
           const uint32_t tv = tb + 2 * j + 1, tk = tb + 2 * j + 2;
           const uint32_t sv = tv % kStages, sk = tk % kStages;
           const bool more = (j + 1 < n);
-          if (!kv_ready(tv) || !mbar_wait(bar(kBarPFull + 0), p_phase[0], wc, kSiteMmaPFull)) {
+          if (!kv_ready(tv) || !mbar_wait(bar(kBarPHalf + 0), p_phase & 1u, wc, kSiteMmaPFull)) {
             ok = false;
             break;
           }
-          p_phase[0] ^= 1u;
           ptx::tc_fence_after();
-          pv(0, sv, j > 0);
+          LLMFA_TRACE_EVENT(kEvMmaPHalf, j);
+          pv_half(0, sv, j > 0, 0);
+          if (!mbar_wait(bar(kBarPFull + 0), p_phase & 1u, wc, kSiteMmaPFull)) {
+            ok = false;
+            break;
+          }
+          ptx::tc_fence_after();
+          LLMFA_TRACE_EVENT(kEvMmaPFull, j);
+          pv_half(0, sv, true, 4);
+          p_phase ^= 1u;
           if (!more) commit_both(kBarOFull + 0);
           if (more) {
             if (!kv_ready(tk)) {
@@ -577,15 +658,22 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
             ptx::tc_fence_after();
             qk(0, sk);
             commit_both(kBarSFull + 0);
+            LLMFA_TRACE_EVENT(kEvMmaQK, j);
             if (j + 2 == n) commit_both(kBarQEmpty + 0);
           }
-          if (!mbar_wait(bar(kBarPFull + 1), p_phase[1], wc, kSiteMmaPFull)) {
+          if (!mbar_wait(bar(kBarPHalf + 1), (p_phase >> 1) & 1u, wc, kSiteMmaPFull)) {
             ok = false;
             break;
           }
-          p_phase[1] ^= 1u;
           ptx::tc_fence_after();
-          pv(1, sv, j > 0);
+          pv_half(1, sv, j > 0, 0);
+          if (!mbar_wait(bar(kBarPFull + 1), (p_phase >> 1) & 1u, wc, kSiteMmaPFull)) {
+            ok = false;
+            break;
+          }
+          ptx::tc_fence_after();
+          pv_half(1, sv, true, 4);
+          p_phase ^= 2u;
           commit_both(kBarKVEmpty + sv);
           if (!more) commit_both(kBarOFull + 1);
           if (more) {

@@ -294,6 +294,25 @@ int llmfa_max_active_clusters(int* out_clusters) {
   return LLMFA_OK;
 }
 
+int llmfa_trace_read(void* dst_host, uint64_t capacity_bytes, uint64_t* written_bytes) {
+  if (dst_host == nullptr || written_bytes == nullptr) return LLMFA_ERR_INVALID_ARGUMENT;
+  *written_bytes = 0;
+#if LLMFA_TRACE
+  const uint64_t bytes = sizeof(llmfa::TraceRecord) * llmfa::kTraceRecords;
+  if (capacity_bytes < bytes) return LLMFA_ERR_INVALID_ARGUMENT;
+  if (cudaDeviceSynchronize() != cudaSuccess ||
+      cudaMemcpyFromSymbol(dst_host, llmfa::g_trace, bytes) != cudaSuccess) {
+    cudaGetLastError();
+    return LLMFA_ERR_CUDA;
+  }
+  *written_bytes = bytes;
+  return LLMFA_OK;
+#else
+  (void)capacity_bytes;
+  return LLMFA_ERR_UNSUPPORTED;
+#endif
+}
+
 int llmfa_selftest_wait_timeout(uint32_t timeout_us, void* stream) {
   if (timeout_us == 0 || timeout_us > 10000000u) return LLMFA_ERR_INVALID_ARGUMENT;
   int dev = 0;
