@@ -205,7 +205,7 @@ def run_ours(args, cfg, world, rank, local):
     import torch
     import torch.distributed as dist
 
-    from llm_fa_b200 import attention_forward, device_status
+    from llm_fa_b200 import attention_forward, device_status, launch_plan
     from llm_fa_b200.workloads import make_inputs
 
     torch.cuda.set_device(local)
@@ -216,6 +216,7 @@ def run_ours(args, cfg, world, rank, local):
     Sk = k_h.shape[1]
     flops_local = 4 * B * H * Sq * Sk * 128
     q, k, v = q_h.to(dev), k_h.to(dev), v_h.to(dev)
+    plan = launch_plan(B, H, Sq, Sk)  # kernels per forward: attention (+ split-KV combine)
     o = torch.empty_like(q)
     flush = torch.empty(L2_FLUSH_BYTES, dtype=torch.uint8, device=dev)
     stream = torch.cuda.current_stream(dev)
@@ -331,7 +332,8 @@ def run_ours(args, cfg, world, rank, local):
                      "peak_source": peak_src,
                      "traffic": PROFILED_TRAFFIC_BYTES.get(cfg.name),
                      "algorithmic_bytes": cfg.io_bytes},
-        "gpu_launches": args.steps,
+        "gpu_launches": args.steps * plan["kernels"],
+        "launch_plan": plan,
         "clocks": clocks,
     }
     if e2e is not None:
@@ -339,7 +341,7 @@ def run_ours(args, cfg, world, rank, local):
                        "h2d_bytes_per_step": e2e["h2d"], "d2h_bytes_per_step": e2e["d2h"],
                        "ms_per_step": round(e2e_ms_max, 4),
                        "path": "llm_fa_b200.attention_forward, pinned host buffers"}
-        line["gpu_launches"] += args.steps
+        line["gpu_launches"] += args.steps * plan["kernels"]
     if world == 1 and not args.no_cpu_baseline:
         line["cpu_baseline"] = cpu_baseline(cfg, args.cpu_seconds)
     return line

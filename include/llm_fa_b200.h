@@ -45,22 +45,35 @@ extern "C" {
  * aligned and strides multiples of 8 elements (16 bytes). Any seq_q >= 1 and
  * seq_k >= 1 are accepted (the reference requires q % 512 == 0,
  * sk % 128 == 0, sk >= 256; llm_fa.cu:1421-1428).
+ * `workspace` (optional, 16-byte aligned, at least llmfa_workspace_size()
+ * bytes; may be NULL) is scratch for the partial results of query blocks
+ * whose KV range is split across SMs when there are too few blocks to fill
+ * the GPU (two launches then: the attention kernel and a combine kernel).
+ * Without it every query block is computed by one SM pair. Its contents
+ * are not read across calls; calls that share a workspace must not overlap.
  * `stream` is a cudaStream_t (NULL = legacy default stream). No device
  * synchronisation; no allocation.
  */
 int llmfa_forward(const void* q, const int64_t q_strides[3], const void* k,
                   const int64_t k_strides[3], const void* v, const int64_t v_strides[3], void* o,
                   const int64_t o_strides[3], int64_t batch, int64_t heads, int64_t seq_q,
-                  int64_t seq_k, float softmax_scale, void* stream);
+                  int64_t seq_k, float softmax_scale, void* workspace, uint64_t workspace_bytes,
+                  void* stream);
+
+/* Workspace bytes that let llmfa_forward split KV ranges on the current
+ * device (depends on the device's SM count only, not on the shapes). No
+ * counterpart in the reference, which always launches one cluster per 512
+ * query rows (llm_fa.cu:1465). */
+int llmfa_workspace_size(uint64_t* bytes);
 
 /*
  * The reference call shape exactly: contiguous row-major Q (seq_q,128),
  * K/V (seq_k,128), O (seq_q,128) bf16, softmax_scale = 1/sqrt(128)
- * (llm_fa.py:57-65, llm_fa.cu:1418-1475). Asynchronous; O must be allocated
- * by the caller.
+ * (llm_fa.py:57-65, llm_fa.cu:1418-1475). Asynchronous; O (and the optional
+ * workspace, as for llmfa_forward) must be allocated by the caller.
  */
 int llmfa_forward_2d(const void* q, const void* k, const void* v, void* o, int64_t seq_q,
-                     int64_t seq_k, void* stream);
+                     int64_t seq_k, void* workspace, uint64_t workspace_bytes, void* stream);
 
 /* Reads (and keeps) the device status word of the current device after
  * synchronising `stream`: 0, or LLMFA_DEVICE_STATUS_TIMEOUT_BASE + wait-site
@@ -78,6 +91,13 @@ int llmfa_set_wait_timeout_ms(uint32_t ms);
 /* Number of 2-CTA clusters of the attention kernel that can be resident at
  * once on the current device (the persistent grid size). */
 int llmfa_max_active_clusters(int* out_clusters);
+
+/* What llmfa_forward would launch for these sizes and this much workspace on
+ * the current device: number of kernels (1, or 2 with the combine kernel),
+ * grid size in 2-CTA clusters, and how many 512-row query blocks get their
+ * KV range split. No counterpart in the reference. */
+int llmfa_launch_plan(int64_t batch, int64_t heads, int64_t seq_q, int64_t seq_k,
+                      uint64_t workspace_bytes, int* kernels, int* clusters, int* split_units);
 
 /* Human-readable text for a status code. */
 const char* llmfa_error_string(int status);

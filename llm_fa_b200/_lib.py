@@ -31,14 +31,19 @@ SIGNATURES = {
     "llmfa_forward": (ctypes.c_int, [
         ctypes.c_void_p, _I64x3, ctypes.c_void_p, _I64x3, ctypes.c_void_p, _I64x3,
         ctypes.c_void_p, _I64x3, ctypes.c_int64, ctypes.c_int64, ctypes.c_int64,
-        ctypes.c_int64, ctypes.c_float, ctypes.c_void_p]),
+        ctypes.c_int64, ctypes.c_float, ctypes.c_void_p, ctypes.c_uint64, ctypes.c_void_p]),
+    "llmfa_workspace_size": (ctypes.c_int, [ctypes.POINTER(ctypes.c_uint64)]),
     "llmfa_forward_2d": (ctypes.c_int, [
         ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p,
-        ctypes.c_int64, ctypes.c_int64, ctypes.c_void_p]),
+        ctypes.c_int64, ctypes.c_int64, ctypes.c_void_p, ctypes.c_uint64, ctypes.c_void_p]),
     "llmfa_device_status": (ctypes.c_int, [ctypes.POINTER(ctypes.c_int), ctypes.c_void_p]),
     "llmfa_reset_device_status": (ctypes.c_int, [ctypes.c_void_p]),
     "llmfa_set_wait_timeout_ms": (ctypes.c_int, [ctypes.c_uint32]),
     "llmfa_max_active_clusters": (ctypes.c_int, [ctypes.POINTER(ctypes.c_int)]),
+    "llmfa_launch_plan": (ctypes.c_int, [ctypes.c_int64, ctypes.c_int64, ctypes.c_int64,
+                                         ctypes.c_int64, ctypes.c_uint64,
+                                         ctypes.POINTER(ctypes.c_int), ctypes.POINTER(ctypes.c_int),
+                                         ctypes.POINTER(ctypes.c_int)]),
     "llmfa_error_string": (ctypes.c_char_p, [ctypes.c_int]),
     "llmfa_version": (ctypes.c_int, []),
     "llmfa_selftest_wait_timeout": (ctypes.c_int, [ctypes.c_uint32, ctypes.c_void_p]),

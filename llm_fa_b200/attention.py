@@ -73,15 +73,35 @@ def attention_forward(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, *,
     scale = (1.0 / math.sqrt(HEAD_DIM)) if softmax_scale is None else float(softmax_scale)
     L = _lib.lib()
     with torch.cuda.device(device):
+        # scratch for split KV ranges, from the caching allocator on this stream
+        ws_bytes = workspace_size(device)
+        ws = torch.empty(ws_bytes, dtype=torch.uint8, device=device)
         stream = torch.cuda.current_stream(device).cuda_stream
         rc = L.llmfa_forward(
             ctypes.c_void_p(q4.data_ptr()), _lib.strides3(q4.stride()[:3]),
             ctypes.c_void_p(k4.data_ptr()), _lib.strides3(k4.stride()[:3]),
             ctypes.c_void_p(v4.data_ptr()), _lib.strides3(v4.stride()[:3]),
             ctypes.c_void_p(o4.data_ptr()), _lib.strides3(o4.stride()[:3]),
-            B, H, Sq, Sk, ctypes.c_float(scale), ctypes.c_void_p(stream))
+            B, H, Sq, Sk, ctypes.c_float(scale), ctypes.c_void_p(ws.data_ptr()), ws_bytes,
+            ctypes.c_void_p(stream))
     _lib.check(rc, "llmfa_forward")
     return out
+
+
+_WS_BYTES: dict[int, int] = {}
+
+
+def workspace_size(device: torch.device | int | None = None) -> int:
+    """Bytes of split-KV scratch llmfa_forward can use on `device` (cached per device)."""
+    idx = torch.cuda.current_device() if device is None else (
+        device if isinstance(device, int) else device.index)
+    got = _WS_BYTES.get(idx)
+    if got is None:
+        out = ctypes.c_uint64(0)
+        with torch.cuda.device(idx):
+            _lib.check(_lib.lib().llmfa_workspace_size(ctypes.byref(out)), "llmfa_workspace_size")
+        got = _WS_BYTES[idx] = int(out.value)
+    return got
 
 
 def device_status(device: torch.device | int | None = None) -> int:
@@ -107,6 +127,18 @@ def reset_device_status(device: torch.device | int | None = None) -> None:
 
 def set_wait_timeout_ms(ms: int) -> None:
     _lib.check(_lib.lib().llmfa_set_wait_timeout_ms(int(ms)), "llmfa_set_wait_timeout_ms")
+
+
+def launch_plan(batch: int, heads: int, seq_q: int, seq_k: int,
+                workspace_bytes: int | None = None) -> dict:
+    """Kernels, clusters and split query blocks of one forward on the current device."""
+    if workspace_bytes is None:
+        workspace_bytes = workspace_size()
+    k, c, s = ctypes.c_int(0), ctypes.c_int(0), ctypes.c_int(0)
+    _lib.check(_lib.lib().llmfa_launch_plan(batch, heads, seq_q, seq_k, workspace_bytes,
+                                            ctypes.byref(k), ctypes.byref(c), ctypes.byref(s)),
+               "llmfa_launch_plan")
+    return {"kernels": k.value, "clusters": c.value, "split_units": s.value}
 
 
 def max_active_clusters() -> int:

@@ -84,17 +84,17 @@ constexpr int kNumBars = kBarDrain + 1;
 
 constexpr uint32_t kSmemScale = kSmemBar + 512;                 // float [2][128]
 constexpr uint32_t kSmemLsum = kSmemScale + kQTiles * kBlockM * 4;  // float [2][128]
-constexpr uint32_t kSmemTmemSlot = kSmemLsum + kQTiles * kBlockM * 4;
-constexpr uint32_t kSmemAbort = kSmemTmemSlot + 4;
-constexpr uint32_t kSmemUsed = kSmemAbort + 4;
+constexpr uint32_t kSmemMrow = kSmemLsum + kQTiles * kBlockM * 4;   // float [2][128]
+constexpr uint32_t kSmemTmemSlot = kSmemMrow + kQTiles * kBlockM * 4;
+constexpr uint32_t kSmemUsed = kSmemTmemSlot + 4;
 constexpr uint32_t kSmemBytes = kSmemUsed + 1024;  // + base-alignment slack
 static_assert(kNumBars * 8 <= 512, "barrier area");
 static_assert(kSmemBytes <= 227 * 1024, "shared memory budget");
 
 // setmaxnreg split of the 65536 registers (launch: 512 threads x 128):
-// 2 softmax warpgroups x 128 x 176 + correction 128 x 64 + control 128 x 96.
-constexpr uint32_t kRegsSoftmax = 176;
-constexpr uint32_t kRegsCorrection = 64;
+// 2 softmax warpgroups x 128 x 168 + correction 128 x 80 + control 128 x 96.
+constexpr uint32_t kRegsSoftmax = 168;
+constexpr uint32_t kRegsCorrection = 80;
 constexpr uint32_t kRegsControl = 96;
 static_assert(2 * 128 * kRegsSoftmax + 128 * kRegsCorrection + 128 * kRegsControl <= 65536,
               "register split exceeds the launch allocation");
@@ -103,7 +103,7 @@ constexpr float kRescaleThreshold = 8.0f;  // log2 units
 // Pairs (bit k = columns 2k, 2k+1) of each 32-column chunk whose exp2 runs on
 // the FMA pipe (softmax_exp2.cuh) instead of MUFU; the rest use ex2.approx.
 #ifndef LLMFA_SOFTMAX_POLY_MASK
-#define LLMFA_SOFTMAX_POLY_MASK 0x8888u
+#define LLMFA_SOFTMAX_POLY_MASK 0x0u
 #endif
 constexpr uint32_t kSoftmaxPolyMask = LLMFA_SOFTMAX_POLY_MASK;
 
@@ -166,6 +166,21 @@ __device__ __forceinline__ void trace_event(int ev, int j, uint32_t rank, int cl
 #define LLMFA_TRACE_EVENT(ev, j) ((void)0)
 #endif
 
+// Where a bounded wait reports a timeout and how long it waits (read only on
+// the slow path, from the kernel's grid-constant parameters).
+struct WaitCtl {
+  int* status;
+  unsigned long long timeout_ns;
+};
+
+// CTA-wide abort flag of the bounded waits (static shared memory: a constant
+// address, so waits keep no register for it).
+__shared__ uint32_t g_cta_abort;
+__device__ __forceinline__ uint32_t cta_aborted() {
+  return *static_cast<volatile uint32_t*>(&g_cta_abort);
+}
+__device__ __forceinline__ void cta_abort() { *static_cast<volatile uint32_t*>(&g_cta_abort) = 1u; }
+
 struct FwdParams {
   int B, H, Sq, Sk;
   int n_qblk;        // ceil(Sq / 512)
@@ -173,15 +188,22 @@ struct FwdParams {
   int n_units;       // B * H * n_qblk
   int kv_tail;       // valid keys in the last KV tile (1..128)
   float scale_log2;  // softmax_scale * log2(e)
-  unsigned long long timeout_ns;
-  int* status;       // device status word
+  WaitCtl wait;      // device status word and wait limit
+  // Work split (see SegIter): units [0, dp_units) round-robin over the
+  // clusters; with sk_mode the remaining units' sk_total = units * n_kv
+  // iterations are cut into sk_clusters contiguous ranges.
+  int sk_mode;
+  int dp_units;
+  int sk_clusters;
+  long long sk_total;
+  float* ws;         // partial-result slots (sk_mode only)
 };
 
-struct WaitCtl {
-  volatile uint32_t* abort;
-  int* status;
-  unsigned long long timeout_ns;
-};
+// Partial-result slot of a unit split across clusters: unnormalised O
+// (512 rows x 128, fp32), then the row max m (log2 units) and row sum l.
+constexpr int kSlotRows = kUnitRows;
+constexpr long long kSlotFloats = static_cast<long long>(kSlotRows) * kHeadDim + 2 * kSlotRows;
+constexpr long long kSlotBytes = kSlotFloats * 4;
 
 // Slow path of a bounded wait. With honor_abort, returns early once another
 // role of this CTA has given up.
@@ -191,9 +213,9 @@ __device__ __forceinline__ bool mbar_wait_slow(uint32_t bar, uint32_t parity, co
   for (uint32_t it = 1;; ++it) {
     if (ptx::mbar_try_wait(bar, parity)) return true;
     if ((it & 63u) == 0) {
-      if (honor_abort && *c.abort) return false;
+      if (honor_abort && cta_aborted()) return false;
       if (ptx::globaltimer_ns() - t0 > c.timeout_ns) {
-        *c.abort = 1u;
+        cta_abort();
         atomicCAS(c.status, 0, kStatusTimeoutBase + site);
         return false;
       }
@@ -222,6 +244,71 @@ __device__ __forceinline__ UnitCoord decode_unit(const FwdParams& p, int u) {
   const int qb = u - bh * p.n_qblk;
   return {bh / p.H, bh % p.H, qb * kUnitRows};
 }
+
+// ---------------------------------------------------------------- work split
+// Work is (unit, KV tile) iterations. Full waves of units go to the clusters
+// round-robin (cluster c: units c, c + G, ...), the classic persistent
+// schedule, which keeps concurrently running clusters on the same (batch,
+// head) so K/V tiles are shared in L2. In stream-K mode the units of the
+// last, partial wave are flattened into their units * n_kv iterations and cut
+// into contiguous ranges, one per cluster, so every SM has the same amount of
+// work; a unit cut across clusters is finished by llm_fa_combine_kernel from
+// the fp32 partial results (O, row max, row sum) of each piece.
+struct Segment {
+  int u;     // unit
+  int j0;    // first KV tile
+  int len;   // number of KV tiles
+  int slot;  // partial-result slot, or -1 when this cluster computes the whole unit
+};
+
+__host__ __device__ __forceinline__ long long sk_begin(long long total, int parts, int c) {
+  return c >= parts ? total : total * c / parts;
+}
+// Cluster whose stream-K range holds iteration `it` (0 <= it < total).
+__host__ __device__ __forceinline__ int sk_owner(long long total, int parts, long long it) {
+  int c = static_cast<int>((it * parts) / total);
+  while (c + 1 < parts && sk_begin(total, parts, c + 1) <= it) ++c;
+  while (c > 0 && sk_begin(total, parts, c) > it) --c;
+  return c;
+}
+
+struct SegIter {
+  int c, G, k;
+  long long it, end;
+  bool first_sk;
+  __device__ __forceinline__ SegIter(const FwdParams& p, int cluster, int nclusters)
+      : c(cluster), G(nclusters), k(0), it(0), end(0), first_sk(true) {
+    if (p.sk_mode) {
+      const long long base = static_cast<long long>(p.dp_units) * p.n_kv;
+      it = base + sk_begin(p.sk_total, p.sk_clusters, c);
+      end = base + sk_begin(p.sk_total, p.sk_clusters, c + 1);
+    }
+  }
+  __device__ __forceinline__ bool next(const FwdParams& p, Segment& s) {
+    const int classic_units = p.sk_mode ? p.dp_units : p.n_units;
+    const int uc = c + k * G;
+    if (uc < classic_units) {
+      s = Segment{uc, 0, p.n_kv, -1};
+      ++k;
+      return true;
+    }
+    if (!p.sk_mode || it >= end) return false;
+    const int u = static_cast<int>(it / p.n_kv);
+    const int j0 = static_cast<int>(it - static_cast<long long>(u) * p.n_kv);
+    const long long rest = end - it;
+    const int len = (p.n_kv - j0) < rest ? (p.n_kv - j0) : static_cast<int>(rest);
+    const bool whole = (j0 == 0 && len == p.n_kv);
+    s = Segment{u, j0, len, whole ? -1 : 2 * c + (first_sk ? 0 : 1)};
+    it += len;
+    first_sk = false;
+    return true;
+  }
+  __device__ __forceinline__ bool has_next(const FwdParams& p) const {
+    SegIter copy = *this;
+    Segment s;
+    return copy.next(p, s);
+  }
+};
 
 // Maximum of 32 scores (raw bits) with independent 3-input max chains.
 __device__ __forceinline__ float chunk_max(const uint32_t (&r)[32]) {
@@ -265,7 +352,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
     llm_fa_kernel_sm100(const __grid_constant__ CUtensorMap tmQ,
                         const __grid_constant__ CUtensorMap tmK,
                         const __grid_constant__ CUtensorMap tmV,
-                        const __grid_constant__ CUtensorMap tmO, const FwdParams p) {
+                        const __grid_constant__ CUtensorMap tmO,
+                        const __grid_constant__ FwdParams p) {
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   const uint32_t smem_base = (ptx::smem_u32(smem_raw) + 1023u) & ~1023u;
   uint8_t* smem_gen = smem_raw + (smem_base - ptx::smem_u32(smem_raw));
@@ -280,8 +368,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
   auto bar = [&](int idx) -> uint32_t { return smem_base + kSmemBar + 8u * idx; };
   float* sm_scale = reinterpret_cast<float*>(smem_gen + kSmemScale);
   float* sm_lsum = reinterpret_cast<float*>(smem_gen + kSmemLsum);
-  volatile uint32_t* abort_flag = reinterpret_cast<volatile uint32_t*>(smem_gen + kSmemAbort);
-  const WaitCtl wc{abort_flag, p.status, p.timeout_ns};
+  float* sm_mrow = reinterpret_cast<float*>(smem_gen + kSmemMrow);
+  const WaitCtl& wc = p.wait;
 
   // ------------------------------------------------------------ prologue
   if (warp == 0 && lane == 0) {
@@ -304,7 +392,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
     ptx::mbar_init(bar(kBarOStageFull), 4);
     ptx::mbar_init(bar(kBarOStageEmpty), 1);
     ptx::mbar_init(bar(kBarDrain), 1);
-    *abort_flag = 0u;
+    g_cta_abort = 0u;
     ptx::fence_mbar_init();
   }
   if (warp == 12) {
@@ -323,7 +411,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
   ptx::tc_fence_after();
   const uint32_t tmem_base = *reinterpret_cast<volatile uint32_t*>(smem_gen + kSmemTmemSlot);
 
-  const int n = p.n_kv;
+  const int n = p.n_kv;  // KV tiles per unit (a segment may cover fewer)
 
   if (warp < 8) {
     // ========================================================== softmax
@@ -339,9 +427,13 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
     const uint64_t c2 = ptx::f2_pack(p.scale_log2, p.scale_log2);
     uint32_t s_phase = 0;
     bool ok = true;
-    for (int u = cluster; u < p.n_units && ok; u += nclusters) {
+    SegIter si(p, cluster, nclusters);
+    Segment sg;
+    while (ok && si.next(p, sg)) {
+      const int u = sg.u;
       float m = 0.f, l = 0.f;
-      for (int j = 0; j < n; ++j) {
+      for (int j = 0; j < sg.len; ++j) {
+        const bool last_tile = (sg.j0 + j == n - 1);
         if (!mbar_wait_warp(bar(kBarSFull + tile), s_phase, wc, kSiteSoftSFull)) {
           ok = false;
           break;
@@ -367,7 +459,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
           ptx::reg_fence32(s2);
           ptx::reg_fence32(s3);
           if (warp == 0 && lane == 0) LLMFA_TRACE_EVENT(kEvLdDone, j);
-          if (j == n - 1) {
+          if (last_tile) {
             mask_tail(s0, 0, p.kv_tail);
             mask_tail(s1, 32, p.kv_tail);
             mask_tail(s2, 64, p.kv_tail);
@@ -410,7 +502,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
           ptx::tmem_wait_ld();
           ptx::reg_fence32(s2);
           ptx::reg_fence32(s3);
-          if (j == n - 1) {
+          if (last_tile) {
             mask_tail(s2, 64, p.kv_tail);
             mask_tail(s3, 96, p.kv_tail);
           }
@@ -427,11 +519,13 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
         if (warp == 0 && lane == 0) LLMFA_TRACE_EVENT(kEvPFull, j);
       }
       if (!ok) break;
+      (void)u;
       sm_lsum[tile * kBlockM + row] = l;
+      sm_mrow[tile * kBlockM + row] = m;
       __syncwarp();
       if (lane == 0) ptx::mbar_arrive(lsum_bar);
     }
-    if (!ok) *abort_flag = 1u;
+    if (!ok) cta_abort();
     // every role returns to the launch register count before the shared teardown
     ptx::setmaxnreg_dec<128>();
   } else if (warp < 12) {
@@ -445,7 +539,10 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
     uint32_t lsum_phase = 0, o_phase = 0, stage_phase = 0;
     bool ok = true;
     bool first = true;
-    for (int u = cluster; u < p.n_units && ok; u += nclusters) {
+    SegIter si(p, cluster, nclusters);
+    Segment sg;
+    while (ok && si.next(p, sg)) {
+      const int u = sg.u;
       const UnitCoord uc = decode_unit(p, u);
       if (first) {
         // j = 0 needs no correction: O_t is overwritten by the unit's first PV.
@@ -456,7 +553,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
         __syncwarp();
         first = false;
       }
-      for (int j = 1; j < n && ok; ++j) {
+      for (int j = 1; j < sg.len && ok; ++j) {
 #pragma unroll 1
         for (int tile = 0; tile < 2; ++tile) {
           if (!mbar_wait_warp(bar(kBarStat + tile * 4 + quarter), (stat_phase >> tile) & 1u, wc,
@@ -497,7 +594,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
         }
       }
       if (!ok) break;
-      const bool has_next = (u + nclusters) < p.n_units;
+      const bool has_next = si.has_next(p);
 #pragma unroll 1
       for (int tile = 0; tile < 2; ++tile) {
         if (!mbar_wait_warp(bar(kBarLsum + tile * 4 + quarter), lsum_phase, wc, kSiteCorrLsum) ||
@@ -507,8 +604,33 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
           break;
         }
         ptx::tc_fence_after();
-        const float inv_l = __frcp_rn(sm_lsum[tile * kBlockM + row]);
         const uint32_t t_o = tmem_base + lane_off + 256 + tile * 128;
+        if (sg.slot >= 0) {
+          // Piece of a unit split across clusters: unnormalised O, m and l to
+          // the partial-result slot; llm_fa_combine_kernel finishes the unit.
+          const int row_u = tile * (kBlockM * kPair) + static_cast<int>(rank) * kBlockM + row;
+          float* slot = p.ws + static_cast<long long>(sg.slot) * kSlotFloats;
+          float* orow_ptr = slot + static_cast<long long>(row_u) * kHeadDim;
+#pragma unroll 1
+          for (int c = 0; c < 4; ++c) {
+            uint32_t r[32];
+            ptx::tmem_ld32(t_o + 32 * c, r);
+            ptx::tmem_wait_ld();
+            ptx::reg_fence32(r);
+#pragma unroll
+            for (int q = 0; q < 8; ++q)
+              *reinterpret_cast<uint4*>(orow_ptr + 32 * c + 4 * q) =
+                  make_uint4(r[4 * q], r[4 * q + 1], r[4 * q + 2], r[4 * q + 3]);
+          }
+          slot[kSlotRows * kHeadDim + row_u] = sm_mrow[tile * kBlockM + row];
+          slot[kSlotRows * kHeadDim + kSlotRows + row_u] = sm_lsum[tile * kBlockM + row];
+          ptx::tc_fence_before();
+          __syncwarp();
+          if (lane == 0 && has_next)
+            ptx::mbar_arrive_cluster(ptx::mapa(bar(kBarPHalf + tile), 0));
+          continue;  // the staging buffer was not used: its barriers keep their phase
+        }
+        const float inv_l = __frcp_rn(sm_lsum[tile * kBlockM + row]);
 #pragma unroll 1
         for (int c = 0; c < 4; ++c) {
           uint32_t r[32];
@@ -561,7 +683,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
       lsum_phase ^= 1u;
       o_phase ^= 1u;
     }
-    if (!ok) *abort_flag = 1u;
+    if (!ok) cta_abort();
     if (warp == 8 && lane == 0) ptx::bulk_wait_group0();
     __syncwarp();
     ptx::setmaxnreg_inc<128>();
@@ -608,7 +730,12 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
       uint32_t kv_t = 0, q_use = 0;
       uint32_t p_phase = 0;  // bit t: phase parity of tile t's P barriers
       bool ok = true;
-      for (int u = cluster; u < p.n_units && ok; u += nclusters) {
+      SegIter si(p, cluster, nclusters);
+      Segment sg;
+      while (ok && si.next(p, sg)) {
+        const int n = sg.len;  // KV tiles of this segment
+        const int u = sg.u;
+        (void)u;
         const uint32_t tb = kv_t;
         const uint32_t sk0 = tb % kStages;
         if (!mbar_wait(bar(kBarQFull + 0), q_use & 1u, wc, kSiteMmaQFull) || !kv_ready(tb)) {
@@ -686,7 +813,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
         kv_t = tb + 2 * n;
         ++q_use;
       }
-      if (!ok) *abort_flag = 1u;
+      if (!ok) cta_abort();
       // Drain: every MMA issued above completes before TMEM is released.
       ptx::mma_commit<2>(bar(kBarDrain));
       mbar_wait(bar(kBarDrain), 0, wc, kSiteDrain, /*honor_abort=*/false);
@@ -696,8 +823,12 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
       const uint64_t pol_kv = ptx::policy_evict_last();
       uint32_t kv_t = 0, q_use = 0;
       bool ok = true;
-      for (int u = cluster; u < p.n_units && ok; u += nclusters) {
-        const UnitCoord uc = decode_unit(p, u);
+      SegIter si(p, cluster, nclusters);
+      Segment sg;
+      while (ok && si.next(p, sg)) {
+        const UnitCoord uc = decode_unit(p, sg.u);
+        const int n = sg.len;
+        const int j0 = sg.j0;
         auto load_q = [&](int tile) -> bool {
           if (!mbar_wait(bar(kBarQEmpty + tile), (q_use & 1u) ^ 1u, wc, kSiteProdQEmpty))
             return false;
@@ -723,7 +854,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
           uint32_t stage, full;
           if (!acquire(stage, full)) return false;
           const uint32_t dst = smem_base + kSmemKV + stage * kKVStageBytes;
-          const int krow = j * kBlockN + static_cast<int>(rank) * (kBlockN / kPair);
+          const int krow = (j0 + j) * kBlockN + static_cast<int>(rank) * (kBlockN / kPair);
           ptx::tma_load_4d<true>(dst, &tmK, full, 0, uc.h, krow, uc.b, pol_kv);
           ptx::tma_load_4d<true>(dst + kKVStageBytes / 2, &tmK, full, 64, uc.h, krow, uc.b,
                                  pol_kv);
@@ -734,7 +865,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
           if (!acquire(stage, full)) return false;
           const uint32_t dst = smem_base + kSmemKV + stage * kKVStageBytes;
           ptx::tma_load_4d<true>(dst, &tmV, full, static_cast<int>(rank) * 64, uc.h,
-                                 j * kBlockN, uc.b, pol_kv);
+                                 (j0 + j) * kBlockN, uc.b, pol_kv);
           return true;
         };
         ok = load_q(0) && load_k(0) && load_q(1);
@@ -745,7 +876,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
         ++q_use;
       }
       if (!ok) {
-        *abort_flag = 1u;
+        cta_abort();
         // let copies already issued land before the CTA's shared memory is released
         const uint64_t t0 = ptx::globaltimer_ns();
         while (ptx::globaltimer_ns() - t0 < 20000ull) {
@@ -764,6 +895,65 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
   if (warp == 12) {
     ptx::tc_fence_after();
     ptx::tmem_dealloc<2>(tmem_base, 512);
+  }
+}
+
+// ---------------------------------------------------------------- combine
+// Finishes the units that stream-K mode cut across clusters: for every query
+// row, O = sum_c 2^(m_c - m) O_c / sum_c 2^(m_c - m) l_c over the pieces c
+// (m = max_c m_c), the standard merge of partial softmax states. One CTA per
+// 128 rows of a stream-K unit, one warp per row (32 lanes x 4 columns).
+struct CombineParams {
+  const float* ws;
+  uint16_t* o;                  // bf16 output, [B, Sq, H, 128] element strides below
+  long long o_sb, o_ss, o_sh;
+  int H, Sq, n_kv, n_qblk, dp_units, sk_clusters;
+  long long sk_total;
+};
+
+__global__ void __launch_bounds__(256) llm_fa_combine_kernel(const __grid_constant__ CombineParams p) {
+  const int unit = p.dp_units + static_cast<int>(blockIdx.x >> 2);
+  const int rb = static_cast<int>(blockIdx.x & 3);
+  const long long base = static_cast<long long>(p.dp_units) * p.n_kv;
+  const long long it_lo = static_cast<long long>(unit) * p.n_kv - base;
+  const int c_lo = sk_owner(p.sk_total, p.sk_clusters, it_lo);
+  const int c_hi = sk_owner(p.sk_total, p.sk_clusters, it_lo + p.n_kv - 1);
+  if (c_lo == c_hi) return;  // one cluster computed the whole unit
+  const int bh = unit / p.n_qblk;
+  const int qb = unit - bh * p.n_qblk;
+  const int b = bh / p.H, h = bh % p.H;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  for (int r = warp; r < 128; r += 8) {
+    const int row_u = rb * 128 + r;
+    const int srow = qb * kUnitRows + row_u;
+    if (srow >= p.Sq) break;
+    float mstar = -INFINITY;
+    for (int c = c_lo; c <= c_hi; ++c) {
+      const long long c0 = sk_begin(p.sk_total, p.sk_clusters, c);
+      if (c0 == sk_begin(p.sk_total, p.sk_clusters, c + 1)) continue;
+      const int slot = 2 * c + (((base + c0) / p.n_kv) == unit ? 0 : 1);
+      mstar = fmaxf(mstar, p.ws[slot * kSlotFloats + kSlotRows * kHeadDim + row_u]);
+    }
+    float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+    float lstar = 0.f;
+    for (int c = c_lo; c <= c_hi; ++c) {
+      const long long c0 = sk_begin(p.sk_total, p.sk_clusters, c);
+      if (c0 == sk_begin(p.sk_total, p.sk_clusters, c + 1)) continue;
+      const int slot = 2 * c + (((base + c0) / p.n_kv) == unit ? 0 : 1);
+      const float* sl = p.ws + slot * kSlotFloats;
+      const float w = exp2f(sl[kSlotRows * kHeadDim + row_u] - mstar);
+      lstar += w * sl[kSlotRows * kHeadDim + kSlotRows + row_u];
+      const float4 v = *reinterpret_cast<const float4*>(sl + row_u * kHeadDim + lane * 4);
+      acc.x += w * v.x;
+      acc.y += w * v.y;
+      acc.z += w * v.z;
+      acc.w += w * v.w;
+    }
+    const float inv = 1.f / lstar;
+    uint2 pk;
+    pk.x = ptx::bf16x2_pack(acc.x * inv, acc.y * inv);
+    pk.y = ptx::bf16x2_pack(acc.z * inv, acc.w * inv);
+    *reinterpret_cast<uint2*>(p.o + b * p.o_sb + srow * p.o_ss + h * p.o_sh + lane * 4) = pk;
   }
 }
 

@@ -148,18 +148,45 @@ int encode_bshd(CUtensorMap* m, const void* ptr, const int64_t* st, int64_t seq,
   return r == CUDA_SUCCESS ? LLMFA_OK : LLMFA_ERR_TENSOR_MAP;
 }
 
+// Launch plan of one forward: classic persistent schedule, or stream-K over
+// the last partial wave of units when a large enough workspace is given and
+// the classic schedule would leave more than 2% of the clusters idle.
+struct Plan {
+  int nclusters;   // grid size in 2-CTA clusters
+  int sk_mode;
+  int dp_units;
+  int sk_clusters;
+  long long sk_total;
+};
+Plan make_plan(int n_units, int n_kv, int G, bool have_workspace) {
+  Plan pl{n_units < G ? n_units : G, 0, 0, 0, 0};
+  const int waves = (n_units + G - 1) / G;
+  const double classic_eff = static_cast<double>(n_units) / (static_cast<double>(G) * waves);
+  if (!have_workspace || classic_eff >= 0.98) return pl;
+  const int dp_units = (n_units / G) * G;
+  const long long sk_total = static_cast<long long>(n_units - dp_units) * n_kv;
+  long long parts = sk_total / 4;  // at least 4 KV tiles per piece
+  if (parts > G) parts = G;
+  if (parts < 2) return pl;
+  pl.sk_mode = 1;
+  pl.dp_units = dp_units;
+  pl.sk_clusters = static_cast<int>(parts);
+  pl.sk_total = sk_total;
+  pl.nclusters = dp_units > 0 ? G : pl.sk_clusters;
+  return pl;
+}
+
 __global__ void llmfa_wait_selftest_kernel(unsigned long long timeout_ns, int* status) {
   __shared__ __align__(8) uint64_t bar;
-  __shared__ uint32_t abort_flag;
   const uint32_t b = llmfa::ptx::smem_u32(&bar);
   if (threadIdx.x == 0) {
     llmfa::ptx::mbar_init(b, 1);
-    abort_flag = 0u;
+    llmfa::g_cta_abort = 0u;
     llmfa::ptx::fence_mbar_init();
   }
   __syncthreads();
   if (threadIdx.x == 0) {
-    const llmfa::WaitCtl c{&abort_flag, status, timeout_ns};
+    const llmfa::WaitCtl c{status, timeout_ns};
     // Nothing arrives on `bar`: phase 0 never completes and the wait gives up.
     if (!llmfa::mbar_wait(b, 0, c, kSiteSelftest, false)) {
       // the status word already holds the wait site
@@ -192,10 +219,21 @@ int llmfa_set_wait_timeout_ms(uint32_t ms) {
   return LLMFA_OK;
 }
 
+int llmfa_workspace_size(uint64_t* bytes) {
+  if (bytes == nullptr) return LLMFA_ERR_INVALID_ARGUMENT;
+  int dev = 0;
+  DeviceSetup* s = nullptr;
+  int rc = device_setup(&dev, &s);
+  if (rc != LLMFA_OK) return rc;
+  *bytes = static_cast<uint64_t>(2 * s->max_clusters) * llmfa::kSlotBytes;
+  return LLMFA_OK;
+}
+
 int llmfa_forward(const void* q, const int64_t q_strides[3], const void* k,
                   const int64_t k_strides[3], const void* v, const int64_t v_strides[3], void* o,
                   const int64_t o_strides[3], int64_t batch, int64_t heads, int64_t seq_q,
-                  int64_t seq_k, float softmax_scale, void* stream) {
+                  int64_t seq_k, float softmax_scale, void* workspace, uint64_t workspace_bytes,
+                  void* stream) {
   // ---- argument checks (no CUDA call before they pass)
   if (batch < 1 || heads < 1 || seq_q < 1 || seq_k < 1) return LLMFA_ERR_INVALID_ARGUMENT;
   if (!(softmax_scale > 0.f) || !std::isfinite(softmax_scale)) return LLMFA_ERR_INVALID_ARGUMENT;
@@ -236,23 +274,52 @@ int llmfa_forward(const void* q, const int64_t q_strides[3], const void* k,
   p.n_units = static_cast<int>(n_units);
   p.kv_tail = static_cast<int>(seq_k - int64_t(p.n_kv - 1) * llmfa::kBlockN);
   p.scale_log2 = softmax_scale * 1.4426950408889634f;
-  p.timeout_ns = wait_timeout_ns();
-  p.status = s->status_ptr;
+  p.wait.timeout_ns = wait_timeout_ns();
+  p.wait.status = s->status_ptr;
 
-  const int nclusters = p.n_units < s->max_clusters ? p.n_units : s->max_clusters;
+  const int G = s->max_clusters;
+  const uint64_t need = static_cast<uint64_t>(2 * G) * llmfa::kSlotBytes;
+  const Plan pl = make_plan(p.n_units, p.n_kv, G,
+                            workspace != nullptr && workspace_bytes >= need && aligned16(workspace));
+  const int nclusters = pl.nclusters;
+  if (pl.sk_mode) {
+    p.sk_mode = 1;
+    p.dp_units = pl.dp_units;
+    p.sk_clusters = pl.sk_clusters;
+    p.sk_total = pl.sk_total;
+    p.ws = static_cast<float*>(workspace);
+  }
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
   llmfa::llm_fa_kernel_sm100<<<dim3(2 * nclusters, 1, 1), dim3(llmfa::kThreads, 1, 1),
-                               llmfa::kSmemBytes, static_cast<cudaStream_t>(stream)>>>(tq, tk, tv,
-                                                                                       to, p);
+                               llmfa::kSmemBytes, st>>>(tq, tk, tv, to, p);
   if (cudaGetLastError() != cudaSuccess) return LLMFA_ERR_LAUNCH;
+  if (p.sk_mode) {
+    llmfa::CombineParams cp{};
+    cp.ws = p.ws;
+    cp.o = static_cast<uint16_t*>(o);
+    cp.o_sb = o_strides[0];
+    cp.o_ss = o_strides[1];
+    cp.o_sh = o_strides[2];
+    cp.H = p.H;
+    cp.Sq = p.Sq;
+    cp.n_kv = p.n_kv;
+    cp.n_qblk = p.n_qblk;
+    cp.dp_units = p.dp_units;
+    cp.sk_clusters = p.sk_clusters;
+    cp.sk_total = p.sk_total;
+    const int blocks = (p.n_units - p.dp_units) * 4;
+    llmfa::llm_fa_combine_kernel<<<blocks, 256, 0, st>>>(cp);
+    if (cudaGetLastError() != cudaSuccess) return LLMFA_ERR_LAUNCH;
+  }
   return LLMFA_OK;
 }
 
 int llmfa_forward_2d(const void* q, const void* k, const void* v, void* o, int64_t seq_q,
-                     int64_t seq_k, void* stream) {
+                     int64_t seq_k, void* workspace, uint64_t workspace_bytes, void* stream) {
   const int64_t sq[3] = {seq_q * 128, 128, 128};
   const int64_t sk[3] = {seq_k * 128, 128, 128};
   return llmfa_forward(q, sq, k, sk, v, sk, o, sq, 1, 1, seq_q, seq_k,
-                       1.0f / std::sqrt(128.0f), stream);
+                       1.0f / std::sqrt(128.0f), workspace, workspace_bytes, stream);
 }
 
 int llmfa_device_status(int* out_status, void* stream) {
@@ -281,6 +348,27 @@ int llmfa_reset_device_status(void* stream) {
     cudaGetLastError();
     return LLMFA_ERR_CUDA;
   }
+  return LLMFA_OK;
+}
+
+int llmfa_launch_plan(int64_t batch, int64_t heads, int64_t seq_q, int64_t seq_k,
+                      uint64_t workspace_bytes, int* kernels, int* clusters, int* split_units) {
+  if (kernels == nullptr || clusters == nullptr || split_units == nullptr || batch < 1 ||
+      heads < 1 || seq_q < 1 || seq_k < 1)
+    return LLMFA_ERR_INVALID_ARGUMENT;
+  int dev = 0;
+  DeviceSetup* s = nullptr;
+  int rc = device_setup(&dev, &s);
+  if (rc != LLMFA_OK) return rc;
+  const int64_t n_qblk = (seq_q + llmfa::kUnitRows - 1) / llmfa::kUnitRows;
+  const int n_units = static_cast<int>(batch * heads * n_qblk);
+  const int n_kv = static_cast<int>((seq_k + llmfa::kBlockN - 1) / llmfa::kBlockN);
+  const int G = s->max_clusters;
+  const Plan pl =
+      make_plan(n_units, n_kv, G, workspace_bytes >= static_cast<uint64_t>(2 * G) * llmfa::kSlotBytes);
+  *kernels = pl.sk_mode ? 2 : 1;
+  *clusters = pl.nclusters;
+  *split_units = pl.sk_mode ? n_units - pl.dp_units : 0;
   return LLMFA_OK;
 }
 

@@ -48,7 +48,7 @@ def _call(L, q=16, k=16, v=16, o=16, qs=(1024 * 128, 128, 128), ks=(1024 * 128, 
     ptr = lambda a: ctypes.c_void_p(a) if a else None  # noqa: E731
     return L.llmfa_forward(ptr(q), _lib.strides3(qs), ptr(k), _lib.strides3(ks), ptr(v),
                            _lib.strides3(ks), ptr(o), _lib.strides3(qs), B, H, Sq, Sk,
-                           ctypes.c_float(scale), None)
+                           ctypes.c_float(scale), None, 0, None)
 
 
 @pytest.mark.parametrize("kw,code", [
@@ -75,6 +75,7 @@ def test_small_helpers_validate(L):
     assert L.llmfa_device_status(None, None) == _lib.LLMFA_ERR_INVALID_ARGUMENT
     assert L.llmfa_max_active_clusters(None) == _lib.LLMFA_ERR_INVALID_ARGUMENT
     assert L.llmfa_selftest_wait_timeout(0, None) == _lib.LLMFA_ERR_INVALID_ARGUMENT
+    assert L.llmfa_workspace_size(None) == _lib.LLMFA_ERR_INVALID_ARGUMENT
 
 
 def test_python_wrapper_rejects_cpu_tensors():

@@ -14,7 +14,9 @@ import pytest
 import torch
 import torch.nn.functional as F
 
-from llm_fa_b200 import _lib, attention_forward, device_status, reset_device_status
+import ctypes
+
+from llm_fa_b200 import _lib, attention_forward, device_status, launch_plan, reset_device_status
 from llm_fa_b200 import llm_fa as mirror
 from llm_fa_b200 import selftest_wait_timeout, set_wait_timeout_ms
 from llm_fa_b200.workloads import CONFIGS, Config, make_inputs, sample_rows
@@ -207,6 +209,46 @@ def test_streams_and_determinism():
     s.synchronize()
     torch.cuda.synchronize()
     assert torch.equal(o1, o2)
+
+
+# ----------------------------------------------------------------- split KV ranges
+def _forward_c_abi(q, k, v, workspace: bool):
+    """llmfa_forward through ctypes with or without the split-KV workspace."""
+    from llm_fa_b200.attention import workspace_size
+    o = torch.empty_like(q)
+    ws_bytes = workspace_size() if workspace else 0
+    ws = torch.empty(max(ws_bytes, 1), dtype=torch.uint8, device=q.device)
+    B, Sq, H, _ = q.shape
+    rc = _lib.lib().llmfa_forward(
+        ctypes.c_void_p(q.data_ptr()), _lib.strides3(q.stride()[:3]),
+        ctypes.c_void_p(k.data_ptr()), _lib.strides3(k.stride()[:3]),
+        ctypes.c_void_p(v.data_ptr()), _lib.strides3(v.stride()[:3]),
+        ctypes.c_void_p(o.data_ptr()), _lib.strides3(o.stride()[:3]),
+        B, H, Sq, k.shape[1], ctypes.c_float(1 / math.sqrt(128)),
+        ctypes.c_void_p(ws.data_ptr() if workspace else 0), ws_bytes,
+        ctypes.c_void_p(torch.cuda.current_stream().cuda_stream))
+    _lib.check(rc, "llmfa_forward")
+    torch.cuda.synchronize()
+    assert device_status() == 0
+    return o.cpu()
+
+
+@pytest.mark.parametrize("B,H,Sq,Sk", [(1, 1, 512, 8192), (1, 2, 1000, 1000), (1, 1, 16384, 4096),
+                                        (2, 3, 700, 2500), (3, 50, 512, 640)])
+def test_split_kv_matches_unsplit_and_oracle(B, H, Sq, Sk):
+    cfg = Config("sk", B, H, Sq, Sk, seed=Sq * 7 + Sk)
+    q, k, v = make_inputs(cfg)
+    plan = launch_plan(B, H, Sq, Sk)
+    if B * H * ((Sq + 511) // 512) < 60:
+        assert plan["kernels"] == 2 and plan["split_units"] > 0, plan
+    qd, kd, vd = q.cuda(), k.cuda(), v.cuda()
+    o_split = _forward_c_abi(qd, kd, vd, workspace=True)
+    o_whole = _forward_c_abi(qd, kd, vd, workspace=False)
+    rows = sample_rows(cfg, 512)
+    ref = sdpa_fp32(q, k, v, rows=rows)
+    _assert_close(o_split[:, rows], ref)
+    _assert_close(o_whole[:, rows], ref)
+    _assert_close(o_split, o_whole.float(), 8e-3, 5e-4)
 
 
 # ----------------------------------------------------------------- reference surface
