@@ -76,16 +76,21 @@ constexpr int kBarPHalf = kBarSFull + 2;            // [2] leader: P_t keys 0-63
 constexpr int kBarPFull = kBarPHalf + 2;            // [2] leader: P_t keys 64-127 written
 constexpr int kBarOFull = kBarPFull + 2;            // [2] each: last PV of the unit done
 constexpr int kBarStat = kBarOFull + 2;             // [2x4] softmax warp -> correction warp
-constexpr int kBarLsum = kBarStat + 8;              // [2x4] final row sums ready
-constexpr int kBarOStageFull = kBarLsum + 8;        // [1] 4 correction warps wrote staging
+constexpr int kBarLsum = kBarStat + 8;              // [2 parity][2x4] end-of-segment row sum/max
+constexpr int kBarOStageFull = kBarLsum + 16;       // [1] 4 correction warps wrote staging
 constexpr int kBarOStageEmpty = kBarOStageFull + 1; // [1] TMA store finished reading staging
 constexpr int kBarDrain = kBarOStageEmpty + 1;      // [1] leader: teardown MMA drain
 constexpr int kNumBars = kBarDrain + 1;
 
 constexpr uint32_t kSmemScale = kSmemBar + 512;                 // float [2][128]
-constexpr uint32_t kSmemLsum = kSmemScale + kQTiles * kBlockM * 4;  // float [2][128]
-constexpr uint32_t kSmemMrow = kSmemLsum + kQTiles * kBlockM * 4;   // float [2][128]
-constexpr uint32_t kSmemTmemSlot = kSmemMrow + kQTiles * kBlockM * 4;
+// End-of-segment row sum and row max, double-buffered by segment parity: the
+// softmax of a one-tile segment can finish before the correction warps have
+// read the previous segment's values (nothing orders a segment's QK after the
+// previous epilogue), but never two segments ahead (the next segment's PV
+// waits for that epilogue). float [parity][tile][128] each.
+constexpr uint32_t kSmemLsum = kSmemScale + kQTiles * kBlockM * 4;
+constexpr uint32_t kSmemMrow = kSmemLsum + 2 * kQTiles * kBlockM * 4;
+constexpr uint32_t kSmemTmemSlot = kSmemMrow + 2 * kQTiles * kBlockM * 4;
 constexpr uint32_t kSmemUsed = kSmemTmemSlot + 4;
 constexpr uint32_t kSmemBytes = kSmemUsed + 1024;  // + base-alignment slack
 static_assert(kNumBars * 8 <= 512, "barrier area");
@@ -388,6 +393,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
     for (int k = 0; k < 8; ++k) {
       ptx::mbar_init(bar(kBarStat + k), 1);
       ptx::mbar_init(bar(kBarLsum + k), 1);
+      ptx::mbar_init(bar(kBarLsum + 8 + k), 1);
     }
     ptx::mbar_init(bar(kBarOStageFull), 4);
     ptx::mbar_init(bar(kBarOStageEmpty), 1);
@@ -423,7 +429,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
     const uint32_t phalf_leader = ptx::mapa(bar(kBarPHalf + tile), 0);
     const uint32_t pfull_leader = ptx::mapa(bar(kBarPFull + tile), 0);
     const uint32_t stat_bar = bar(kBarStat + tile * 4 + quarter);
-    const uint32_t lsum_bar = bar(kBarLsum + tile * 4 + quarter);
+    uint32_t seg_parity = 0;  // selects the row sum/max buffer and barrier of this segment
     const uint64_t c2 = ptx::f2_pack(p.scale_log2, p.scale_log2);
     uint32_t s_phase = 0;
     bool ok = true;
@@ -520,10 +526,11 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
       }
       if (!ok) break;
       (void)u;
-      sm_lsum[tile * kBlockM + row] = l;
-      sm_mrow[tile * kBlockM + row] = m;
+      sm_lsum[(seg_parity * kQTiles + tile) * kBlockM + row] = l;
+      sm_mrow[(seg_parity * kQTiles + tile) * kBlockM + row] = m;
       __syncwarp();
-      if (lane == 0) ptx::mbar_arrive(lsum_bar);
+      if (lane == 0) ptx::mbar_arrive(bar(kBarLsum + seg_parity * 8 + tile * 4 + quarter));
+      seg_parity ^= 1u;
     }
     if (!ok) cta_abort();
     // every role returns to the launch register count before the shared teardown
@@ -536,7 +543,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
     const uint32_t lane_off = static_cast<uint32_t>(quarter * 32) << 16;
     const uint32_t sO = smem_base + kSmemO;
     uint32_t stat_phase = 0;  // bit t: phase parity of the tile-t stat barrier
-    uint32_t lsum_phase = 0, o_phase = 0, stage_phase = 0;
+    uint32_t seg_count = 0, o_phase = 0, stage_phase = 0;
     bool ok = true;
     bool first = true;
     SegIter si(p, cluster, nclusters);
@@ -597,7 +604,10 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
       const bool has_next = si.has_next(p);
 #pragma unroll 1
       for (int tile = 0; tile < 2; ++tile) {
-        if (!mbar_wait_warp(bar(kBarLsum + tile * 4 + quarter), lsum_phase, wc, kSiteCorrLsum) ||
+        // buffer seg_count & 1, barrier phase (seg_count >> 1) & 1
+        const uint32_t sp = seg_count & 1u;
+        if (!mbar_wait_warp(bar(kBarLsum + sp * 8 + tile * 4 + quarter), (seg_count >> 1) & 1u, wc,
+                            kSiteCorrLsum) ||
             !mbar_wait_warp(bar(kBarOFull + tile), o_phase, wc, kSiteEpiOFull) ||
             !mbar_wait_warp(bar(kBarOStageEmpty), stage_phase ^ 1u, wc, kSiteEpiStage)) {
           ok = false;
@@ -622,15 +632,16 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
               *reinterpret_cast<uint4*>(orow_ptr + 32 * c + 4 * q) =
                   make_uint4(r[4 * q], r[4 * q + 1], r[4 * q + 2], r[4 * q + 3]);
           }
-          slot[kSlotRows * kHeadDim + row_u] = sm_mrow[tile * kBlockM + row];
-          slot[kSlotRows * kHeadDim + kSlotRows + row_u] = sm_lsum[tile * kBlockM + row];
+          slot[kSlotRows * kHeadDim + row_u] = sm_mrow[(sp * kQTiles + tile) * kBlockM + row];
+          slot[kSlotRows * kHeadDim + kSlotRows + row_u] =
+              sm_lsum[(sp * kQTiles + tile) * kBlockM + row];
           ptx::tc_fence_before();
           __syncwarp();
           if (lane == 0 && has_next)
             ptx::mbar_arrive_cluster(ptx::mapa(bar(kBarPHalf + tile), 0));
           continue;  // the staging buffer was not used: its barriers keep their phase
         }
-        const float inv_l = __frcp_rn(sm_lsum[tile * kBlockM + row]);
+        const float inv_l = __frcp_rn(sm_lsum[(sp * kQTiles + tile) * kBlockM + row]);
 #pragma unroll 1
         for (int c = 0; c < 4; ++c) {
           uint32_t r[32];
@@ -680,7 +691,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
           break;
         }
       }
-      lsum_phase ^= 1u;
+      ++seg_count;
       o_phase ^= 1u;
     }
     if (!ok) cta_abort();

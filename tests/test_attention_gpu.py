@@ -233,8 +233,12 @@ def _forward_c_abi(q, k, v, workspace: bool):
     return o.cpu()
 
 
+# (1, 1, 2048, 2176): a cluster's one-tile segment follows a multi-tile one, the case
+# where the end-of-segment row sums must not be overwritten before they are read;
+# (2, 64, 1024, 100): many one-tile units per cluster in the round-robin part.
 @pytest.mark.parametrize("B,H,Sq,Sk", [(1, 1, 512, 8192), (1, 2, 1000, 1000), (1, 1, 16384, 4096),
-                                        (2, 3, 700, 2500), (3, 50, 512, 640)])
+                                        (2, 3, 700, 2500), (3, 50, 512, 640), (1, 1, 2048, 2176),
+                                        (1, 2, 2000, 2049), (2, 64, 1024, 100)])
 def test_split_kv_matches_unsplit_and_oracle(B, H, Sq, Sk):
     cfg = Config("sk", B, H, Sq, Sk, seed=Sq * 7 + Sk)
     q, k, v = make_inputs(cfg)
