@@ -281,7 +281,7 @@ struct SegIter {
   int c, G, k;
   long long it, end;
   bool first_sk;
-  __device__ __forceinline__ SegIter(const FwdParams& p, int cluster, int nclusters)
+  __host__ __device__ __forceinline__ SegIter(const FwdParams& p, int cluster, int nclusters)
       : c(cluster), G(nclusters), k(0), it(0), end(0), first_sk(true) {
     if (p.sk_mode) {
       const long long base = static_cast<long long>(p.dp_units) * p.n_kv;
@@ -289,7 +289,7 @@ struct SegIter {
       end = base + sk_begin(p.sk_total, p.sk_clusters, c + 1);
     }
   }
-  __device__ __forceinline__ bool next(const FwdParams& p, Segment& s) {
+  __host__ __device__ __forceinline__ bool next(const FwdParams& p, Segment& s) {
     const int classic_units = p.sk_mode ? p.dp_units : p.n_units;
     const int uc = c + k * G;
     if (uc < classic_units) {
@@ -308,7 +308,7 @@ struct SegIter {
     first_sk = false;
     return true;
   }
-  __device__ __forceinline__ bool has_next(const FwdParams& p) const {
+  __host__ __device__ __forceinline__ bool has_next(const FwdParams& p) const {
     SegIter copy = *this;
     Segment s;
     return copy.next(p, s);
@@ -912,8 +912,9 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
 // ---------------------------------------------------------------- combine
 // Finishes the units that stream-K mode cut across clusters: for every query
 // row, O = sum_c 2^(m_c - m) O_c / sum_c 2^(m_c - m) l_c over the pieces c
-// (m = max_c m_c), the standard merge of partial softmax states. One CTA per
-// 128 rows of a stream-K unit, one warp per row (32 lanes x 4 columns).
+// (m = max_c m_c), the standard merge of partial softmax states. Memory-bound:
+// one thread per (row, 4 columns), 8 rows per CTA, 64 CTAs per unit, so the
+// loads of all rows are in flight together.
 struct CombineParams {
   const float* ws;
   uint16_t* o;                  // bf16 output, [B, Sq, H, 128] element strides below
@@ -921,51 +922,87 @@ struct CombineParams {
   int H, Sq, n_kv, n_qblk, dp_units, sk_clusters;
   long long sk_total;
 };
+constexpr int kCombineRowsPerCta = 8;
+constexpr int kCombineMaxPieces = 160;  // >= clusters a unit can be cut across
+
+__host__ __device__ __forceinline__ int combine_slot(const CombineParams& p, int c, int unit,
+                                            long long base) {
+  const long long c0 = sk_begin(p.sk_total, p.sk_clusters, c);
+  return 2 * c + (((base + c0) / p.n_kv) == unit ? 0 : 1);
+}
 
 __global__ void __launch_bounds__(256) llm_fa_combine_kernel(const __grid_constant__ CombineParams p) {
-  const int unit = p.dp_units + static_cast<int>(blockIdx.x >> 2);
-  const int rb = static_cast<int>(blockIdx.x & 3);
-  const long long base = static_cast<long long>(p.dp_units) * p.n_kv;
-  const long long it_lo = static_cast<long long>(unit) * p.n_kv - base;
-  const int c_lo = sk_owner(p.sk_total, p.sk_clusters, it_lo);
-  const int c_hi = sk_owner(p.sk_total, p.sk_clusters, it_lo + p.n_kv - 1);
-  if (c_lo == c_hi) return;  // one cluster computed the whole unit
+  constexpr int kCtasPerUnit = kUnitRows / kCombineRowsPerCta;
+  const int unit = p.dp_units + static_cast<int>(blockIdx.x / kCtasPerUnit);
+  const int row_u = static_cast<int>(blockIdx.x % kCtasPerUnit) * kCombineRowsPerCta +
+                    static_cast<int>(threadIdx.x >> 5);
+  const int lane = threadIdx.x & 31;
+  // The pieces of this unit (their partial-result slots), found once per CTA.
+  __shared__ int s_slot[kCombineMaxPieces];
+  __shared__ int s_npieces;
+  if (threadIdx.x == 0) {
+    const long long base = static_cast<long long>(p.dp_units) * p.n_kv;
+    const long long it_lo = static_cast<long long>(unit) * p.n_kv - base;
+    const int c_lo = sk_owner(p.sk_total, p.sk_clusters, it_lo);
+    const int c_hi = sk_owner(p.sk_total, p.sk_clusters, it_lo + p.n_kv - 1);
+    int np = 0;
+    if (c_lo != c_hi)  // otherwise one cluster computed the whole unit
+      for (int c = c_lo; c <= c_hi && np < kCombineMaxPieces; ++c)
+        s_slot[np++] = combine_slot(p, c, unit, base);
+    s_npieces = np;
+  }
+  __syncthreads();
+  const int np = s_npieces;
+  if (np == 0) return;
   const int bh = unit / p.n_qblk;
   const int qb = unit - bh * p.n_qblk;
+  const int srow = qb * kUnitRows + row_u;
+  if (srow >= p.Sq) return;
   const int b = bh / p.H, h = bh % p.H;
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  for (int r = warp; r < 128; r += 8) {
-    const int row_u = rb * 128 + r;
-    const int srow = qb * kUnitRows + row_u;
-    if (srow >= p.Sq) break;
-    float mstar = -INFINITY;
-    for (int c = c_lo; c <= c_hi; ++c) {
-      const long long c0 = sk_begin(p.sk_total, p.sk_clusters, c);
-      if (c0 == sk_begin(p.sk_total, p.sk_clusters, c + 1)) continue;
-      const int slot = 2 * c + (((base + c0) / p.n_kv) == unit ? 0 : 1);
-      mstar = fmaxf(mstar, p.ws[slot * kSlotFloats + kSlotRows * kHeadDim + row_u]);
-    }
-    float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
-    float lstar = 0.f;
-    for (int c = c_lo; c <= c_hi; ++c) {
-      const long long c0 = sk_begin(p.sk_total, p.sk_clusters, c);
-      if (c0 == sk_begin(p.sk_total, p.sk_clusters, c + 1)) continue;
-      const int slot = 2 * c + (((base + c0) / p.n_kv) == unit ? 0 : 1);
-      const float* sl = p.ws + slot * kSlotFloats;
-      const float w = exp2f(sl[kSlotRows * kHeadDim + row_u] - mstar);
-      lstar += w * sl[kSlotRows * kHeadDim + kSlotRows + row_u];
-      const float4 v = *reinterpret_cast<const float4*>(sl + row_u * kHeadDim + lane * 4);
-      acc.x += w * v.x;
-      acc.y += w * v.y;
-      acc.z += w * v.z;
-      acc.w += w * v.w;
-    }
-    const float inv = 1.f / lstar;
-    uint2 pk;
-    pk.x = ptx::bf16x2_pack(acc.x * inv, acc.y * inv);
-    pk.y = ptx::bf16x2_pack(acc.z * inv, acc.w * inv);
-    *reinterpret_cast<uint2*>(p.o + b * p.o_sb + srow * p.o_ss + h * p.o_sh + lane * 4) = pk;
+  constexpr long long kM = static_cast<long long>(kSlotRows) * kHeadDim;
+  // Pieces are visited four at a time so their loads are in flight together.
+  float mstar = -INFINITY;
+  for (int i0 = 0; i0 < np; i0 += 4) {
+    float mv[4];
+#pragma unroll
+    for (int k = 0; k < 4; ++k)
+      mv[k] = (i0 + k < np) ? p.ws[s_slot[i0 + k] * kSlotFloats + kM + row_u] : -INFINITY;
+#pragma unroll
+    for (int k = 0; k < 4; ++k) mstar = fmaxf(mstar, mv[k]);
   }
+  float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+  float lstar = 0.f;
+  for (int i0 = 0; i0 < np; i0 += 4) {
+    float mv[4], lv[4];
+    float4 ov[4];
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+      if (i0 + k < np) {
+        const float* sl = p.ws + s_slot[i0 + k] * kSlotFloats;
+        mv[k] = sl[kM + row_u];
+        lv[k] = sl[kM + kSlotRows + row_u];
+        ov[k] = *reinterpret_cast<const float4*>(sl + row_u * kHeadDim + lane * 4);
+      } else {
+        mv[k] = -INFINITY;
+        lv[k] = 0.f;
+        ov[k] = make_float4(0.f, 0.f, 0.f, 0.f);
+      }
+    }
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+      const float w = exp2f(mv[k] - mstar);
+      lstar += w * lv[k];
+      acc.x += w * ov[k].x;
+      acc.y += w * ov[k].y;
+      acc.z += w * ov[k].z;
+      acc.w += w * ov[k].w;
+    }
+  }
+  const float inv = 1.f / lstar;
+  uint2 pk;
+  pk.x = ptx::bf16x2_pack(acc.x * inv, acc.y * inv);
+  pk.y = ptx::bf16x2_pack(acc.z * inv, acc.w * inv);
+  *reinterpret_cast<uint2*>(p.o + b * p.o_sb + srow * p.o_ss + h * p.o_sh + lane * 4) = pk;
 }
 
 }  // namespace llmfa

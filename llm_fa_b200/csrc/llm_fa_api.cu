@@ -167,6 +167,7 @@ Plan make_plan(int n_units, int n_kv, int G, bool have_workspace) {
   const long long sk_total = static_cast<long long>(n_units - dp_units) * n_kv;
   long long parts = sk_total / 4;  // at least 4 KV tiles per piece
   if (parts > G) parts = G;
+  if (parts > llmfa::kCombineMaxPieces) parts = llmfa::kCombineMaxPieces;
   if (parts < 2) return pl;
   pl.sk_mode = 1;
   pl.dp_units = dp_units;
@@ -307,7 +308,7 @@ int llmfa_forward(const void* q, const int64_t q_strides[3], const void* k,
     cp.dp_units = p.dp_units;
     cp.sk_clusters = p.sk_clusters;
     cp.sk_total = p.sk_total;
-    const int blocks = (p.n_units - p.dp_units) * 4;
+    const int blocks = (p.n_units - p.dp_units) * (llmfa::kUnitRows / llmfa::kCombineRowsPerCta);
     llmfa::llm_fa_combine_kernel<<<blocks, 256, 0, st>>>(cp);
     if (cudaGetLastError() != cudaSuccess) return LLMFA_ERR_LAUNCH;
   }
