@@ -116,6 +116,29 @@ int llmfa_version(void);
 int llmfa_trace_read(void* dst_host, uint64_t capacity_bytes, uint64_t* written_bytes);
 
 /*
+ * llmfa_forward without a workspace argument and without allocating: for
+ * callers that cannot allocate device memory themselves (a foreign-language
+ * host that only holds device pointers handed to it, or a framework that
+ * plans all device memory up front and forbids allocation on the request
+ * path). The split-KV scratch comes from a fixed 39.4 MB array inside this
+ * library (148 partial-result slots: two per 2-SM cluster of a 148-SM B200),
+ * which every GPU that loads the library keeps until the process exits.
+ * Returns LLMFA_ERR_UNSUPPORTED on a device that would need more slots than
+ * that. The first call on each device looks up the array's device address
+ * (cudaGetSymbolAddress, with that device current); make that first call
+ * before any stream capture. All calls share the one array, so calls that
+ * overlap on the GPU (other streams, other host threads) race on it and must
+ * be serialised by the caller. The array's contents from the last call are
+ * left in place; nothing in it has to start at zero. Other arguments and
+ * results as for llmfa_forward. No counterpart in the reference.
+ */
+int llmfa_forward_static_scratch(const void* q, const int64_t q_strides[3], const void* k,
+                                 const int64_t k_strides[3], const void* v,
+                                 const int64_t v_strides[3], void* o, const int64_t o_strides[3],
+                                 int64_t batch, int64_t heads, int64_t seq_q, int64_t seq_k,
+                                 float softmax_scale, void* stream);
+
+/*
  * Failure-detection self test: launches one CTA whose single mbarrier wait can
  * never complete (nothing arrives on it); the bounded wait gives up after
  * `timeout_us` microseconds and records LLMFA_DEVICE_STATUS_TIMEOUT_BASE +

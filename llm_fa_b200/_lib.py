@@ -33,6 +33,10 @@ SIGNATURES = {
         ctypes.c_void_p, _I64x3, ctypes.c_int64, ctypes.c_int64, ctypes.c_int64,
         ctypes.c_int64, ctypes.c_float, ctypes.c_void_p, ctypes.c_uint64, ctypes.c_void_p]),
     "llmfa_workspace_size": (ctypes.c_int, [ctypes.POINTER(ctypes.c_uint64)]),
+    "llmfa_forward_static_scratch": (ctypes.c_int, [
+        ctypes.c_void_p, _I64x3, ctypes.c_void_p, _I64x3, ctypes.c_void_p, _I64x3,
+        ctypes.c_void_p, _I64x3, ctypes.c_int64, ctypes.c_int64, ctypes.c_int64,
+        ctypes.c_int64, ctypes.c_float, ctypes.c_void_p]),
     "llmfa_forward_2d": (ctypes.c_int, [
         ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p,
         ctypes.c_int64, ctypes.c_int64, ctypes.c_void_p, ctypes.c_uint64, ctypes.c_void_p]),

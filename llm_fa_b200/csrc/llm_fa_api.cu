@@ -415,3 +415,62 @@ int llmfa_selftest_wait_timeout(uint32_t timeout_us, void* stream) {
 }
 
 }  // extern "C"
+
+// ---------------------------------------------------------------- allocation-free entry point
+// For callers that cannot allocate device memory themselves: a foreign-language
+// host (Go, Java, Rust over FFI) that was handed device pointers but has no
+// CUDA allocator of its own, or a serving framework that pre-plans every byte
+// of device memory at start-up and forbids allocations on the request path.
+// They get the split-KV scratch from this fixed array instead of a workspace
+// argument. It is sized for one 148-SM B200 (two partial-result slots per
+// 2-SM cluster, 74 clusters): 148 x 266,240 bytes = 39.4 MB, held by every
+// GPU that loads this library until the process exits.
+namespace {
+
+constexpr int kStaticScratchSlots = 148;
+static __device__ __align__(256) float g_static_scratch[kStaticScratchSlots * llmfa::kSlotFloats];
+
+struct StaticScratch {
+  std::once_flag once;
+  int err = LLMFA_OK;
+  float* ptr = nullptr;  // device address of g_static_scratch on this device
+};
+StaticScratch g_static_scratch_dev[kMaxDevices];
+
+}  // namespace
+
+extern "C" int llmfa_forward_static_scratch(const void* q, const int64_t q_strides[3], const void* k,
+                                            const int64_t k_strides[3], const void* v,
+                                            const int64_t v_strides[3], void* o,
+                                            const int64_t o_strides[3], int64_t batch,
+                                            int64_t heads, int64_t seq_q, int64_t seq_k,
+                                            float softmax_scale, void* stream) {
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices) {
+    cudaGetLastError();
+    return LLMFA_ERR_CUDA;
+  }
+  // Once per device, with that device current: the host-side name of the
+  // array is not a device address, so look the address up and keep it.
+  StaticScratch& ss = g_static_scratch_dev[dev];
+  std::call_once(ss.once, [&] {
+    void* ptr = nullptr;
+    if (cudaGetSymbolAddress(&ptr, g_static_scratch) != cudaSuccess || ptr == nullptr) {
+      cudaGetLastError();
+      ss.err = LLMFA_ERR_CUDA;
+      return;
+    }
+    ss.ptr = static_cast<float*>(ptr);
+  });
+  if (ss.err != LLMFA_OK) return ss.err;
+  // The split needs two slots per cluster of this device; refuse rather than
+  // overrun the fixed array on a GPU with more SMs than it was sized for.
+  uint64_t need = 0;
+  const int rc = llmfa_workspace_size(&need);
+  if (rc != LLMFA_OK) return rc;
+  if (need > sizeof(g_static_scratch)) return LLMFA_ERR_UNSUPPORTED;
+  // Nothing in the scratch needs to start at zero: every slot the combine
+  // kernel reads is written by the attention kernel earlier in the same call.
+  return llmfa_forward(q, q_strides, k, k_strides, v, v_strides, o, o_strides, batch, heads, seq_q,
+                       seq_k, softmax_scale, ss.ptr, sizeof(g_static_scratch), stream);
+}
