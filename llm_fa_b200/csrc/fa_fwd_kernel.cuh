@@ -25,7 +25,7 @@
 // Warp roles (16 warps, 512 threads):
 //   0-3  softmax, tile 0          4-7  softmax, tile 1
 //   8-11 correction (O rescale) + epilogue (x 1/l, bf16, TMA store)
-//   12   MMA issue (leader CTA) + TMEM allocation
+//   12   MMA issue (leader CTA, whole warp, one elected lane issues) + TMEM allocation
 //   13   TMA producer             14-15 idle
 //
 // The pair is persistent: cluster c processes units c, c + nclusters, ... in
@@ -131,44 +131,50 @@ enum WaitSite : int {
 // ---------------------------------------------------------------- event trace
 // Intra-kernel event trace, compiled out unless LLMFA_TRACE=1. Cluster 0
 // records, for KV iterations [kTraceFirst, kTraceFirst + kTraceIters) of its
-// first unit and Q tile 0, the %globaltimer (ns) and %clock64 of each hand-off
-// below in both CTAs of the pair. Layout: [cta rank][event][iteration].
+// first unit, the %globaltimer (ns) and %clock64 of each hand-off below, for
+// both Q tiles, in both CTAs of the pair.
+// Layout: [cta rank][Q tile][event][iteration].
 #ifndef LLMFA_TRACE
 #define LLMFA_TRACE 0
 #endif
 constexpr int kTraceFirst = 32;
 constexpr int kTraceIters = 16;
 enum TraceEvent : int {
-  kEvSReady = 0,     // softmax: S_0(j) visible (after the s_full wait)
+  kEvSReady = 0,     // softmax: S_t(j) visible (after the s_full wait)
   kEvLdDone,         // softmax: 128 scores in registers
   kEvStat,           // softmax: rescale factor published
   kEvPHalf,          // softmax: P keys 0-63 published
   kEvPFull,          // softmax: P keys 64-127 published
   kEvMmaPHalf,       // MMA: saw P half (about to issue PV k-steps 0-3)
   kEvMmaPFull,       // MMA: saw P full (about to issue PV k-steps 4-7)
-  kEvMmaQK,          // MMA: QK_0(j+1) issued and committed
+  kEvMmaQK,          // MMA: QK_t(j+1) issued and committed
   kEvCorrStat,       // correction: saw the rescale factor
   kEvCorrArrive,     // correction: arrived on P half
+  kEvMmaKV,          // MMA: V_j ready (tile 0 slot) / K_{j+1} ready (tile 1 slot)
+  kEvProdLoad,       // producer: V_j load issued (tile 0 slot) / K_{j+1} (tile 1 slot)
+  kEvKVLanded,       // observer: V_j landed (tile 0 slot) / K_{j+1} landed (tile 1 slot)
+  kEvMmaLoopTop,     // MMA: top of iteration j (tile 0) / QK_1(j+1) issued, not committed (tile 1)
   kNumTraceEvents
 };
 struct TraceRecord {
   unsigned long long globaltimer_ns;
   long long clock;
 };
-constexpr int kTraceRecords = 2 * kNumTraceEvents * kTraceIters;
+constexpr int kTraceRecords = 2 * kQTiles * kNumTraceEvents * kTraceIters;
 #if LLMFA_TRACE
 __device__ TraceRecord g_trace[kTraceRecords];
-__device__ __forceinline__ void trace_event(int ev, int j, uint32_t rank, int cluster, int u) {
+__device__ __forceinline__ void trace_event(int ev, int tile, int j, uint32_t rank, int cluster,
+                                            int u) {
   if (cluster == 0 && u == 0 && j >= kTraceFirst && j < kTraceFirst + kTraceIters) {
     long long c;
     asm volatile("mov.u64 %0, %%clock64;" : "=l"(c));
-    g_trace[(rank * kNumTraceEvents + ev) * kTraceIters + (j - kTraceFirst)] =
+    g_trace[((rank * kQTiles + tile) * kNumTraceEvents + ev) * kTraceIters + (j - kTraceFirst)] =
         TraceRecord{ptx::globaltimer_ns(), c};
   }
 }
-#define LLMFA_TRACE_EVENT(ev, j) trace_event((ev), (j), rank, cluster, u)
+#define LLMFA_TRACE_EVENT(ev, tile, j) trace_event((ev), (tile), (j), rank, cluster, u)
 #else
-#define LLMFA_TRACE_EVENT(ev, j) ((void)0)
+#define LLMFA_TRACE_EVENT(ev, tile, j) ((void)0)
 #endif
 
 // Where a bounded wait reports a timeout and how long it waits (read only on
@@ -445,7 +451,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
           break;
         }
         s_phase ^= 1u;
-        if (warp == 0 && lane == 0) LLMFA_TRACE_EVENT(kEvSReady, j);
+        if (quarter == 0 && lane == 0) LLMFA_TRACE_EVENT(kEvSReady, tile, j);
         ptx::tc_fence_after();
         // Pass 1: all 128 scores -> row max. Chunks 0-1 stay in registers;
         // chunks 2-3 (columns 64-127, never overwritten by P) are re-read from
@@ -464,7 +470,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
           ptx::reg_fence32(s1);
           ptx::reg_fence32(s2);
           ptx::reg_fence32(s3);
-          if (warp == 0 && lane == 0) LLMFA_TRACE_EVENT(kEvLdDone, j);
+          if (quarter == 0 && lane == 0) LLMFA_TRACE_EVENT(kEvLdDone, tile, j);
           if (last_tile) {
             mask_tail(s0, 0, p.kv_tail);
             mask_tail(s1, 32, p.kv_tail);
@@ -486,7 +492,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
           sm_scale[tile * kBlockM + row] = sc;
           __syncwarp();
           if (lane == 0) ptx::mbar_arrive(stat_bar);
-          if (warp == 0 && lane == 0) LLMFA_TRACE_EVENT(kEvStat, j);
+          if (quarter == 0 && lane == 0) LLMFA_TRACE_EVENT(kEvStat, tile, j);
         }
         // Pass 2: P = exp2(s * scale*log2e - m) -> bf16 -> TMEM columns [0, 64),
         // published in two halves so the first four PV k-steps (keys 0-63)
@@ -504,7 +510,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
           ptx::tc_fence_before();
           __syncwarp();
           if (lane == 0) ptx::mbar_arrive_cluster(phalf_leader);
-          if (warp == 0 && lane == 0) LLMFA_TRACE_EVENT(kEvPHalf, j);
+          if (quarter == 0 && lane == 0) LLMFA_TRACE_EVENT(kEvPHalf, tile, j);
           ptx::tmem_wait_ld();
           ptx::reg_fence32(s2);
           ptx::reg_fence32(s3);
@@ -522,7 +528,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
         ptx::tc_fence_before();
         __syncwarp();
         if (lane == 0) ptx::mbar_arrive_cluster(pfull_leader);
-        if (warp == 0 && lane == 0) LLMFA_TRACE_EVENT(kEvPFull, j);
+        if (quarter == 0 && lane == 0) LLMFA_TRACE_EVENT(kEvPFull, tile, j);
       }
       if (!ok) break;
       (void)u;
@@ -569,7 +575,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
             break;
           }
           stat_phase ^= 1u << tile;
-          if (warp == 8 && lane == 0 && tile == 0) LLMFA_TRACE_EVENT(kEvCorrStat, j);
+          if (warp == 8 && lane == 0) LLMFA_TRACE_EVENT(kEvCorrStat, tile, j);
           const float sc = sm_scale[tile * kBlockM + row];
           if (__any_sync(0xffffffffu, sc != 1.f)) {
             // O_t is quiescent here: PV_t(j-1) completed before S_t(j) was
@@ -597,7 +603,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
           ptx::tc_fence_before();
           __syncwarp();
           if (lane == 0) ptx::mbar_arrive_cluster(ptx::mapa(bar(kBarPHalf + tile), 0));
-          if (warp == 8 && lane == 0 && tile == 0) LLMFA_TRACE_EVENT(kEvCorrArrive, j);
+          if (warp == 8 && lane == 0) LLMFA_TRACE_EVENT(kEvCorrArrive, tile, j);
         }
       }
       if (!ok) break;
@@ -700,26 +706,36 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
     ptx::setmaxnreg_inc<128>();
   } else {
     ptx::setmaxnreg_dec<kRegsControl>();
-    if (warp == 12 && leader && lane == 0) {
+    if (warp == 12 && leader) {
+      // The whole warp runs this role; one elected lane issues each tcgen05
+      // instruction (ptx::mma_*_warp), which keeps the issue path short.
       // ======================================================== MMA issue
       const uint32_t idesc_qk = ptx::idesc_bf16_f32(kBlockM * kPair, kBlockN, false, false);
       const uint32_t idesc_pv = ptx::idesc_bf16_f32(kBlockM * kPair, kHeadDim, false, true);
-      auto commit_both = [&](int b) {
-        ptx::mma_commit<2>(bar(b));
-        ptx::mma_commit<2>(ptx::mapa(bar(b), 1));
+      // Barrier addresses in this CTA and, for the commits that signal both
+      // CTAs, the same offsets in the peer CTA's window.
+      const uint32_t bar_local = bar(0);
+      const uint32_t bar_peer = ptx::mapa(bar_local, 1);
+      auto commit_both = [&](uint32_t b) {
+        ptx::mma_commit_warp(bar_local + 8u * b);
+        ptx::mma_commit_warp(bar_peer + 8u * b);
       };
       // Descriptors: the high half (SBO 1024 B, version, 128-byte swizzle) is
-      // shared; the low half advances by (byte offset >> 4) per K step.
+      // shared; the low half advances by (byte offset >> 4) per K step and by
+      // kKVStageBytes >> 4 per K/V stage.
       const uint32_t dhi = ptx::smem_desc_sw128_hi(1024);
+      const uint32_t q_lo = ptx::smem_desc_lo(smem_base + kSmemQ, 16);
+      const uint32_t k_lo = ptx::smem_desc_lo(smem_base + kSmemKV, 16);
+      const uint32_t v_lo = ptx::smem_desc_lo(smem_base + kSmemKV, kKVStageBytes);
       auto qk = [&](int tile, uint32_t stage) {
         const uint32_t d = tmem_base + tile * 128;
-        const uint32_t alo = ptx::smem_desc_lo(smem_base + kSmemQ + tile * kQTileBytes, 16);
-        const uint32_t blo = ptx::smem_desc_lo(smem_base + kSmemKV + stage * kKVStageBytes, 16);
+        const uint32_t alo = q_lo + tile * (kQTileBytes >> 4);
+        const uint32_t blo = k_lo + stage * (kKVStageBytes >> 4);
 #pragma unroll
         for (int kk = 0; kk < 8; ++kk) {
           const uint32_t aoff = ((kk >> 2) * kPanelBytes + (kk & 3) * 32) >> 4;
           const uint32_t boff = ((kk >> 2) * (kKVStageBytes / 2) + (kk & 3) * 32) >> 4;
-          ptx::mma_ss<2>(d, ptx::make_desc(alo + aoff, dhi), ptx::make_desc(blo + boff, dhi),
+          ptx::mma_ss_warp(d, ptx::make_desc(alo + aoff, dhi), ptx::make_desc(blo + boff, dhi),
                          idesc_qk, kk > 0 ? 1u : 0u);
         }
       };
@@ -727,107 +743,136 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
       auto pv_half = [&](int tile, uint32_t stage, bool acc, int k0) {
         const uint32_t d = tmem_base + 256 + tile * 128;
         const uint32_t pa = tmem_base + tile * 128;
-        const uint32_t vlo =
-            ptx::smem_desc_lo(smem_base + kSmemKV + stage * kKVStageBytes, kKVStageBytes);
+        const uint32_t vlo = v_lo + stage * (kKVStageBytes >> 4);
 #pragma unroll
         for (int kk = k0; kk < k0 + 4; ++kk) {
-          ptx::mma_ts<2>(d, pa + kk * 8, ptx::make_desc(vlo + ((kk * 16 * 128) >> 4), dhi),
+          ptx::mma_ts_warp(d, pa + kk * 8, ptx::make_desc(vlo + ((kk * 16 * 128) >> 4), dhi),
                          idesc_pv, (acc || kk > 0) ? 1u : 0u);
         }
       };
-      auto kv_ready = [&](uint32_t t) -> bool {
-        return mbar_wait(bar(kBarKVFull + t % kStages), (t / kStages) & 1u, wc, kSiteMmaKVFull);
+      // K/V ring: stages are consumed in load order (K_0, V_0, K_1, V_1, ...);
+      // bit s of kv_par is the parity of the next kv_full phase of stage s.
+      uint32_t kv_stage = 0, kv_par = 0;
+      auto kv_take = [&](uint32_t& stage) -> bool {
+        stage = kv_stage;
+        kv_stage = (kv_stage + 1 == kStages) ? 0u : kv_stage + 1;
+        const bool r = mbar_wait_warp(bar_local + 8u * (kBarKVFull + stage), (kv_par >> stage) & 1u, wc,
+                                 kSiteMmaKVFull);
+        kv_par ^= 1u << stage;
+        return r;
       };
-      uint32_t kv_t = 0, q_use = 0;
+      uint32_t q_use = 0;
       uint32_t p_phase = 0;  // bit t: phase parity of tile t's P barriers
       bool ok = true;
       SegIter si(p, cluster, nclusters);
       Segment sg;
+      // The thread blocks in tcgen05.mma while the tensor pipe's queue is
+      // full, so work placed between two MMA groups is a pipe bubble unless
+      // MMAs are still queued. Waits on data that landed long ago (K/V tiles)
+      // are therefore taken before the preceding group is issued, and stage
+      // releases are committed after the following group's first MMAs.
       while (ok && si.next(p, sg)) {
         const int n = sg.len;  // KV tiles of this segment
         const int u = sg.u;
         (void)u;
-        const uint32_t tb = kv_t;
-        const uint32_t sk0 = tb % kStages;
-        if (!mbar_wait(bar(kBarQFull + 0), q_use & 1u, wc, kSiteMmaQFull) || !kv_ready(tb)) {
+        uint32_t sk, sv;
+        if (!mbar_wait_warp(bar_local + 8u * (kBarQFull + 0), q_use & 1u, wc, kSiteMmaQFull) ||
+            !kv_take(sk)) {
           ok = false;
           break;
         }
         ptx::tc_fence_after();
-        qk(0, sk0);
+        qk(0, sk);
         commit_both(kBarSFull + 0);
-        if (!mbar_wait(bar(kBarQFull + 1), q_use & 1u, wc, kSiteMmaQFull)) {
+        if (!mbar_wait_warp(bar_local + 8u * (kBarQFull + 1), q_use & 1u, wc, kSiteMmaQFull)) {
           ok = false;
           break;
         }
         ptx::tc_fence_after();
-        qk(1, sk0);
+        qk(1, sk);
         commit_both(kBarSFull + 1);
-        commit_both(kBarKVEmpty + sk0);
         if (n == 1) {
           commit_both(kBarQEmpty + 0);
           commit_both(kBarQEmpty + 1);
         }
+        if (!kv_take(sv)) {  // V_0
+          ok = false;
+          break;
+        }
+        uint32_t sv_prev = kStages;  // no V stage to release yet
         for (int j = 0; j < n; ++j) {
-          const uint32_t tv = tb + 2 * j + 1, tk = tb + 2 * j + 2;
-          const uint32_t sv = tv % kStages, sk = tk % kStages;
           const bool more = (j + 1 < n);
-          if (!kv_ready(tv) || !mbar_wait(bar(kBarPHalf + 0), p_phase & 1u, wc, kSiteMmaPFull)) {
+          LLMFA_TRACE_EVENT(kEvMmaLoopTop, 0, j);
+          if (!mbar_wait_warp(bar_local + 8u * (kBarPHalf + 0), p_phase & 1u, wc, kSiteMmaPFull)) {
             ok = false;
             break;
           }
           ptx::tc_fence_after();
-          LLMFA_TRACE_EVENT(kEvMmaPHalf, j);
+          LLMFA_TRACE_EVENT(kEvMmaPHalf, 0, j);
           pv_half(0, sv, j > 0, 0);
-          if (!mbar_wait(bar(kBarPFull + 0), p_phase & 1u, wc, kSiteMmaPFull)) {
+          // K_j (last read by QK_1(j)) and V_{j-1} (last read by PV_1(j-1)) are free.
+          commit_both(kBarKVEmpty + sk);
+          if (sv_prev < kStages) commit_both(kBarKVEmpty + sv_prev);
+          if (!mbar_wait_warp(bar_local + 8u * (kBarPFull + 0), p_phase & 1u, wc, kSiteMmaPFull)) {
             ok = false;
             break;
           }
           ptx::tc_fence_after();
-          LLMFA_TRACE_EVENT(kEvMmaPFull, j);
+          LLMFA_TRACE_EVENT(kEvMmaPFull, 0, j);
           pv_half(0, sv, true, 4);
           p_phase ^= 1u;
           if (!more) commit_both(kBarOFull + 0);
           if (more) {
-            if (!kv_ready(tk)) {
+            if (!kv_take(sk)) {  // K_{j+1}
               ok = false;
               break;
             }
+            LLMFA_TRACE_EVENT(kEvMmaKV, 1, j);
             ptx::tc_fence_after();
             qk(0, sk);
             commit_both(kBarSFull + 0);
-            LLMFA_TRACE_EVENT(kEvMmaQK, j);
+            LLMFA_TRACE_EVENT(kEvMmaQK, 0, j);
             if (j + 2 == n) commit_both(kBarQEmpty + 0);
           }
-          if (!mbar_wait(bar(kBarPHalf + 1), (p_phase >> 1) & 1u, wc, kSiteMmaPFull)) {
+          if (!mbar_wait_warp(bar_local + 8u * (kBarPHalf + 1), (p_phase >> 1) & 1u, wc, kSiteMmaPFull)) {
             ok = false;
             break;
           }
           ptx::tc_fence_after();
+          LLMFA_TRACE_EVENT(kEvMmaPHalf, 1, j);
           pv_half(1, sv, j > 0, 0);
-          if (!mbar_wait(bar(kBarPFull + 1), (p_phase >> 1) & 1u, wc, kSiteMmaPFull)) {
+          if (!mbar_wait_warp(bar_local + 8u * (kBarPFull + 1), (p_phase >> 1) & 1u, wc, kSiteMmaPFull)) {
             ok = false;
             break;
           }
           ptx::tc_fence_after();
+          LLMFA_TRACE_EVENT(kEvMmaPFull, 1, j);
           pv_half(1, sv, true, 4);
           p_phase ^= 2u;
-          commit_both(kBarKVEmpty + sv);
-          if (!more) commit_both(kBarOFull + 1);
-          if (more) {
-            qk(1, sk);
-            commit_both(kBarSFull + 1);
-            commit_both(kBarKVEmpty + sk);
-            if (j + 2 == n) commit_both(kBarQEmpty + 1);
+          if (!more) {
+            commit_both(kBarOFull + 1);
+            commit_both(kBarKVEmpty + sv);  // V_{n-1}; K_{n-1} was released above
+            break;
           }
+          sv_prev = sv;
+          if (!kv_take(sv)) {  // V_{j+1}
+            ok = false;
+            break;
+          }
+          LLMFA_TRACE_EVENT(kEvMmaKV, 0, j + 1);
+          qk(1, sk);
+          LLMFA_TRACE_EVENT(kEvMmaLoopTop, 1, j);
+          commit_both(kBarSFull + 1);
+          LLMFA_TRACE_EVENT(kEvMmaQK, 1, j);
+          if (j + 2 == n) commit_both(kBarQEmpty + 1);
         }
-        kv_t = tb + 2 * n;
         ++q_use;
       }
       if (!ok) cta_abort();
       // Drain: every MMA issued above completes before TMEM is released.
-      ptx::mma_commit<2>(bar(kBarDrain));
+      ptx::mma_commit_warp(bar(kBarDrain));
       mbar_wait(bar(kBarDrain), 0, wc, kSiteDrain, /*honor_abort=*/false);
+      __syncwarp();
     } else if (warp == 13 && lane == 0) {
       // ======================================================== TMA producer
       const uint64_t pol_q = ptx::policy_evict_first();
@@ -882,7 +927,13 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
         ok = load_q(0) && load_k(0) && load_q(1);
         for (int j = 0; j < n && ok; ++j) {
           ok = load_v(j);
-          if (ok && j + 1 < n) ok = load_k(j + 1);
+          const int u = sg.u;
+          (void)u;
+          LLMFA_TRACE_EVENT(kEvProdLoad, 0, j);
+          if (ok && j + 1 < n) {
+            ok = load_k(j + 1);
+            LLMFA_TRACE_EVENT(kEvProdLoad, 1, j);
+          }
         }
         ++q_use;
       }
@@ -894,6 +945,28 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
         }
       }
     }
+#if LLMFA_TRACE
+    else if (warp == 14 && lane == 0 && leader && cluster == 0) {
+      // Trace-only observer: when the K/V stages of the traced window land.
+      SegIter si(p, cluster, nclusters);
+      Segment sg;
+      if (si.next(p, sg)) {
+        const int u = sg.u;
+        const int jmax = min(sg.len, kTraceFirst + kTraceIters);
+        for (int j = 0; j < jmax; ++j) {
+          const uint32_t tv = 2 * j + 1, tk = 2 * j + 2;
+          if (!mbar_wait(bar(kBarKVFull + tv % kStages), (tv / kStages) & 1u, wc, kSiteMmaKVFull))
+            break;
+          LLMFA_TRACE_EVENT(kEvKVLanded, 0, j);
+          if (j + 1 < sg.len) {
+            if (!mbar_wait(bar(kBarKVFull + tk % kStages), (tk / kStages) & 1u, wc, kSiteMmaKVFull))
+              break;
+            LLMFA_TRACE_EVENT(kEvKVLanded, 1, j);
+          }
+        }
+      }
+    }
+#endif
     __syncwarp();
     ptx::setmaxnreg_inc<128>();
   }

@@ -2,8 +2,8 @@
 
 Counterpart of the reference's profiler ring (profiler.cuh:44-151) and its
 Perfetto dumper (trace_dump.py:98-325): instead of a per-warp ring flushed
-with atomics, the traced build records fixed hand-off events of Q tile 0 for
-a window of KV iterations of cluster 0 (see TraceEvent in fa_fwd_kernel.cuh).
+with atomics, the traced build records fixed hand-off events of both Q tiles
+for a window of KV iterations of cluster 0 (see TraceEvent in fa_fwd_kernel.cuh).
 Output is a Chrome trace-event JSON (chrome://tracing, Perfetto UI) and a
 table of per-hop latencies; no third-party tracing package is needed.
 """
@@ -17,69 +17,112 @@ import numpy as np
 from . import _lib
 
 EVENTS = ["s_ready", "ld_done", "stat", "p_half", "p_full", "mma_p_half", "mma_p_full",
-          "mma_qk_next", "corr_stat", "corr_arrive"]
+          "mma_qk_next", "corr_stat", "corr_arrive", "mma_kv_ready", "prod_load", "kv_landed",
+          "mma_loop_top"]
+ROLES = {"s_ready": "softmax", "ld_done": "softmax", "stat": "softmax", "p_half": "softmax",
+         "p_full": "softmax", "mma_p_half": "mma", "mma_p_full": "mma", "mma_qk_next": "mma",
+         "corr_stat": "correction", "corr_arrive": "correction", "mma_kv_ready": "mma",
+         "prod_load": "producer", "kv_landed": "producer", "mma_loop_top": "mma"}
 TRACE_FIRST = 32
 TRACE_ITERS = 16
 RECORD = np.dtype([("globaltimer_ns", "<u8"), ("clock", "<i8")])
 
 
 def read_trace() -> np.ndarray:
-    """Structured array [cta rank 2][event][iteration] of (globaltimer_ns, clock)."""
-    n = 2 * len(EVENTS) * TRACE_ITERS
+    """Structured array [cta rank 2][Q tile 2][event][iteration] of (globaltimer_ns, clock)."""
+    n = 2 * 2 * len(EVENTS) * TRACE_ITERS
     buf = np.zeros(n, dtype=RECORD)
     written = ctypes.c_uint64(0)
     rc = _lib.lib().llmfa_trace_read(ctypes.c_void_p(buf.ctypes.data), buf.nbytes,
                                      ctypes.byref(written))
     _lib.check(rc, "llmfa_trace_read (library built without LLMFA_TRACE=1?)")
-    return buf.reshape(2, len(EVENTS), TRACE_ITERS)
+    return buf.reshape(2, 2, len(EVENTS), TRACE_ITERS)
+
+
+def clock_ghz(tr: np.ndarray) -> float:
+    """SM clock estimated from the trace: slope of %clock64 against %globaltimer."""
+    g = tr["globaltimer_ns"].astype(np.float64)
+    c = tr["clock"].astype(np.float64)
+    out = []
+    for r in (0, 1):  # clock64 offsets differ per SM
+        m = g[r] > 0
+        if m.sum() > 2:
+            gx, cx = g[r][m], c[r][m]
+            out.append(np.polyfit(gx - gx.mean(), cx - cx.mean(), 1)[0])
+    return float(np.mean(out)) if out else float("nan")
 
 
 def hop_latencies(tr: np.ndarray, clock_ghz: float) -> dict[str, float]:
-    """Median latency (ns) of each hand-off of the tile-0 pipeline."""
+    """Median latency (ns) of each hand-off of the pipeline, per CTA and Q tile.
+
+    Intra-CTA hops use %clock64 divided by `clock_ghz`; the cross-CTA hop (the
+    peer's P reaching the leader's MMA warp) uses %globaltimer, whose
+    resolution on B200 is 32 ns.
+    """
     E = {e: i for i, e in enumerate(EVENTS)}
 
-    def clk(rank, ev):
-        return tr[rank, E[ev]]["clock"].astype(np.float64) / clock_ghz
+    def clk(rank, tile, ev):
+        return tr[rank, tile, E[ev]]["clock"].astype(np.float64) / clock_ghz
 
-    def gt(rank, ev):
-        return tr[rank, E[ev]]["globaltimer_ns"].astype(np.float64)
+    def gt(rank, tile, ev):
+        return tr[rank, tile, E[ev]]["globaltimer_ns"].astype(np.float64)
 
     out = {}
     for r in (0, 1):
-        out[f"cta{r}: S visible -> scores in registers"] = np.median(clk(r, "ld_done") - clk(r, "s_ready"))
-        out[f"cta{r}: scores -> rescale factor published"] = np.median(clk(r, "stat") - clk(r, "ld_done"))
-        out[f"cta{r}: rescale published -> P half"] = np.median(clk(r, "p_half") - clk(r, "stat"))
-        out[f"cta{r}: P half -> P full"] = np.median(clk(r, "p_full") - clk(r, "p_half"))
-        out[f"cta{r}: period (S visible to S visible)"] = np.median(np.diff(clk(r, "s_ready")))
-        out[f"cta{r}: correction sees rescale factor after it is published"] = np.median(
-            clk(r, "corr_stat") - clk(r, "stat"))
-    out["cta0: P half (own softmax) -> MMA sees P half"] = np.median(clk(0, "mma_p_half") - clk(0, "p_half"))
-    out["cta0: P full (own softmax) -> MMA sees P full"] = np.median(clk(0, "mma_p_full") - clk(0, "p_full"))
-    out["cta1->cta0 (globaltimer): P full -> MMA sees P full"] = np.median(gt(0, "mma_p_full") - gt(1, "p_full"))
-    out["cta0: MMA sees P full -> QK(j+1) issued"] = np.median(clk(0, "mma_qk_next") - clk(0, "mma_p_full"))
-    out["cta0: QK(j+1) issued -> softmax sees S(j+1)"] = np.median(clk(0, "s_ready")[1:] - clk(0, "mma_qk_next")[:-1])
+        for t in (0, 1):
+            k = f"cta{r} tile{t}: "
+            out[k + "S visible -> scores in registers"] = np.median(clk(r, t, "ld_done") - clk(r, t, "s_ready"))
+            out[k + "scores -> rescale factor published"] = np.median(clk(r, t, "stat") - clk(r, t, "ld_done"))
+            out[k + "rescale published -> P half"] = np.median(clk(r, t, "p_half") - clk(r, t, "stat"))
+            out[k + "P half -> P full"] = np.median(clk(r, t, "p_full") - clk(r, t, "p_half"))
+            out[k + "softmax (S visible -> P full)"] = np.median(clk(r, t, "p_full") - clk(r, t, "s_ready"))
+            out[k + "period (S visible to S visible)"] = np.median(np.diff(clk(r, t, "s_ready")))
+            out[k + "correction sees rescale factor after it is published"] = np.median(
+                clk(r, t, "corr_stat") - clk(r, t, "stat"))
+    for t in (0, 1):
+        k = f"tile{t}: "
+        out[k + "cta0 P half -> MMA sees P half"] = np.median(clk(0, t, "mma_p_half") - clk(0, t, "p_half"))
+        out[k + "cta0 P full -> MMA sees P full"] = np.median(clk(0, t, "mma_p_full") - clk(0, t, "p_full"))
+        out[k + "cta1 P full -> MMA sees P full (globaltimer)"] = np.median(
+            gt(0, t, "mma_p_full") - gt(1, t, "p_full"))
+        out[k + "MMA sees P full -> QK(j+1) issued"] = np.median(clk(0, t, "mma_qk_next") - clk(0, t, "mma_p_full"))
+        out[k + "QK(j+1) issued -> softmax sees S(j+1)"] = np.median(
+            clk(0, t, "s_ready")[1:] - clk(0, t, "mma_qk_next")[:-1])
+        out[k + "K/V load issued -> landed"] = np.median(clk(0, t, "kv_landed") - clk(0, t, "prod_load"))
+    out["tile1 S visible - tile0 S visible (same j)"] = np.median(clk(0, 1, "s_ready") - clk(0, 0, "s_ready"))
     return {k: float(v) for k, v in out.items()}
 
 
+def timeline(tr: np.ndarray, clock_ghz: float, rank: int = 0, first: int = 4, count: int = 2):
+    """(ns since S_0 visible at window iteration `first`, label) for CTA `rank`, sorted."""
+    base = tr[rank, 0, 0]["clock"][first]
+    rows = []
+    for i in range(first, min(first + count, TRACE_ITERS)):
+        for t in (0, 1):
+            for e, name in enumerate(EVENTS):
+                c = tr[rank, t, e]["clock"][i]
+                if tr[rank, t, e]["globaltimer_ns"][i]:
+                    rows.append(((c - base) / clock_ghz, f"it{TRACE_FIRST + i} tile{t} {name}"))
+    return sorted(rows)
+
+
 def to_chrome_json(tr: np.ndarray, path: str, clock_ghz: float) -> None:
-    """Instant events per role (pid = CTA rank, tid = role), times in microseconds."""
-    roles = {"s_ready": "softmax", "ld_done": "softmax", "stat": "softmax", "p_half": "softmax",
-             "p_full": "softmax", "mma_p_half": "mma", "mma_p_full": "mma", "mma_qk_next": "mma",
-             "corr_stat": "correction", "corr_arrive": "correction"}
-    t0 = min(int(tr[r, e]["globaltimer_ns"][i]) for r in range(2) for e in range(len(EVENTS))
-             for i in range(TRACE_ITERS) if tr[r, e]["globaltimer_ns"][i] > 0)
+    """Instant events per role and tile (pid = CTA rank, tid = role/tile), times in microseconds."""
+    valid = tr["globaltimer_ns"] > 0
+    t0 = int(tr["globaltimer_ns"][valid].min())
     events = []
     for r in range(2):
-        base_clk = tr[r, 0]["clock"][0]
-        base_gt = tr[r, 0]["globaltimer_ns"][0]
-        for e, name in enumerate(EVENTS):
-            for i in range(TRACE_ITERS):
-                if tr[r, e]["globaltimer_ns"][i] == 0:
-                    continue
-                # clock64 for precise intra-CTA spacing, anchored on the CTA's globaltimer
-                t_ns = (base_gt - t0) + (tr[r, e]["clock"][i] - base_clk) / clock_ghz
-                events.append({"name": name, "ph": "i", "s": "t", "pid": f"cta{r}",
-                               "tid": roles[name], "ts": t_ns / 1e3,
-                               "args": {"iteration": TRACE_FIRST + i}})
+        anchor = tr[r, 0, 0][0]
+        base_clk, base_gt = int(anchor["clock"]), int(anchor["globaltimer_ns"])
+        for t in range(2):
+            for e, name in enumerate(EVENTS):
+                for i in range(TRACE_ITERS):
+                    if tr[r, t, e]["globaltimer_ns"][i] == 0:
+                        continue
+                    # clock64 for precise intra-CTA spacing, anchored on the CTA's globaltimer
+                    t_ns = (base_gt - t0) + (int(tr[r, t, e]["clock"][i]) - base_clk) / clock_ghz
+                    events.append({"name": name, "ph": "i", "s": "t", "pid": f"cta{r}",
+                                   "tid": f"{ROLES[name]} tile{t}", "ts": t_ns / 1e3,
+                                   "args": {"iteration": TRACE_FIRST + i}})
     with open(path, "w") as f:
         json.dump({"traceEvents": events, "displayTimeUnit": "ns"}, f)
