@@ -977,6 +977,9 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
   __syncwarp();
 
   // ------------------------------------------------------------ teardown
+  // A programmatically dependent launch (the combine kernel) may be scheduled
+  // once every CTA got here; it still waits for this grid to complete.
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
   ptx::tc_fence_before();
   __syncthreads();
   ptx::cluster_sync();
@@ -987,99 +990,117 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
 }
 
 // ---------------------------------------------------------------- combine
+// Pieces of stream-K unit u: the clusters [c_lo, c_hi] whose ranges meet it.
+// A piece's slot is 2c when the unit is the first segment of cluster c's
+// range and 2c + 1 when it is the last (a range holds at most two partial
+// segments); only c_lo's range can start before the unit.
+struct UnitPieces {
+  int c_lo, c_hi, slot_lo;
+};
+__host__ __device__ __forceinline__ UnitPieces unit_pieces(const FwdParams& p, int u) {
+  const long long base = static_cast<long long>(p.dp_units) * p.n_kv;
+  const long long it_lo = static_cast<long long>(u) * p.n_kv - base;
+  UnitPieces r;
+  r.c_lo = sk_owner(p.sk_total, p.sk_clusters, it_lo);
+  r.c_hi = sk_owner(p.sk_total, p.sk_clusters, it_lo + p.n_kv - 1);
+  r.slot_lo = 2 * r.c_lo + (sk_begin(p.sk_total, p.sk_clusters, r.c_lo) < it_lo ? 1 : 0);
+  return r;
+}
+__host__ __device__ __forceinline__ int piece_slot(int c_lo, int slot_lo, int c) {
+  return c == c_lo ? slot_lo : 2 * c;
+}
+
 // Finishes the units that stream-K mode cut across clusters: for every query
-// row, O = sum_c 2^(m_c - m) O_c / sum_c 2^(m_c - m) l_c over the pieces c
-// (m = max_c m_c), the standard merge of partial softmax states. Memory-bound:
-// one thread per (row, 4 columns), 8 rows per CTA, 64 CTAs per unit, so the
-// loads of all rows are in flight together.
+// row, O = sum_p 2^(m_p - m) O_p / sum_p 2^(m_p - m) l_p over the pieces p
+// (m = max_p m_p), the standard merge of partial softmax states. The host
+// lists the split units and their pieces. A warp merges 4 rows, one float4
+// column group per lane (coalesced 512-byte rows); the loads of up to four
+// pieces are issued together, and more pieces are folded in groups of four
+// with a running maximum, so a warp waits on memory about once per group.
+constexpr int kCombineMaxUnits = 160;  // > clusters of any B200 grid (split units < clusters)
+constexpr int kCombineRowsPerWarp = 4;
+constexpr int kCombineWarpsPerCta = 8;
 struct CombineParams {
   const float* ws;
   uint16_t* o;                  // bf16 output, [B, Sq, H, 128] element strides below
   long long o_sb, o_ss, o_sh;
-  int H, Sq, n_kv, n_qblk, dp_units, sk_clusters;
-  long long sk_total;
+  int H, Sq, n_qblk, n_split;
+  int unit[kCombineMaxUnits];   // split units
+  short c_lo[kCombineMaxUnits], np[kCombineMaxUnits], slot_lo[kCombineMaxUnits];
 };
-constexpr int kCombineRowsPerCta = 8;
-constexpr int kCombineMaxPieces = 160;  // >= clusters a unit can be cut across
 
-__host__ __device__ __forceinline__ int combine_slot(const CombineParams& p, int c, int unit,
-                                            long long base) {
-  const long long c0 = sk_begin(p.sk_total, p.sk_clusters, c);
-  return 2 * c + (((base + c0) / p.n_kv) == unit ? 0 : 1);
-}
-
-__global__ void __launch_bounds__(256) llm_fa_combine_kernel(const __grid_constant__ CombineParams p) {
-  constexpr int kCtasPerUnit = kUnitRows / kCombineRowsPerCta;
-  const int unit = p.dp_units + static_cast<int>(blockIdx.x / kCtasPerUnit);
-  const int row_u = static_cast<int>(blockIdx.x % kCtasPerUnit) * kCombineRowsPerCta +
-                    static_cast<int>(threadIdx.x >> 5);
+__global__ void __launch_bounds__(kCombineWarpsPerCta * 32)
+    llm_fa_combine_kernel(const __grid_constant__ CombineParams p) {
+  // Launched as a programmatic dependent of the attention kernel: everything
+  // before this wait overlaps that kernel's tail; nothing is read before it.
+  asm volatile("griddepcontrol.wait;" ::: "memory");
+  constexpr int kWarpsPerUnit = kUnitRows / kCombineRowsPerWarp;
   const int lane = threadIdx.x & 31;
-  // The pieces of this unit (their partial-result slots), found once per CTA.
-  __shared__ int s_slot[kCombineMaxPieces];
-  __shared__ int s_npieces;
-  if (threadIdx.x == 0) {
-    const long long base = static_cast<long long>(p.dp_units) * p.n_kv;
-    const long long it_lo = static_cast<long long>(unit) * p.n_kv - base;
-    const int c_lo = sk_owner(p.sk_total, p.sk_clusters, it_lo);
-    const int c_hi = sk_owner(p.sk_total, p.sk_clusters, it_lo + p.n_kv - 1);
-    int np = 0;
-    if (c_lo != c_hi)  // otherwise one cluster computed the whole unit
-      for (int c = c_lo; c <= c_hi && np < kCombineMaxPieces; ++c)
-        s_slot[np++] = combine_slot(p, c, unit, base);
-    s_npieces = np;
-  }
-  __syncthreads();
-  const int np = s_npieces;
-  if (np == 0) return;
-  const int bh = unit / p.n_qblk;
-  const int qb = unit - bh * p.n_qblk;
-  const int srow = qb * kUnitRows + row_u;
-  if (srow >= p.Sq) return;
-  const int b = bh / p.H, h = bh % p.H;
+  const int gw = blockIdx.x * kCombineWarpsPerCta + static_cast<int>(threadIdx.x >> 5);
+  const int i = gw / kWarpsPerUnit;
+  if (i >= p.n_split) return;
+  const int u = p.unit[i];
+  const int c_lo = p.c_lo[i], np = p.np[i], slot_lo = p.slot_lo[i];
+  const int row0 = (gw - i * kWarpsPerUnit) * kCombineRowsPerWarp;
   constexpr long long kM = static_cast<long long>(kSlotRows) * kHeadDim;
-  // Pieces are visited four at a time so their loads are in flight together.
-  float mstar = -INFINITY;
-  for (int i0 = 0; i0 < np; i0 += 4) {
-    float mv[4];
+  float m[kCombineRowsPerWarp], l[kCombineRowsPerWarp];
+  float4 acc[kCombineRowsPerWarp];
 #pragma unroll
-    for (int k = 0; k < 4; ++k)
-      mv[k] = (i0 + k < np) ? p.ws[s_slot[i0 + k] * kSlotFloats + kM + row_u] : -INFINITY;
-#pragma unroll
-    for (int k = 0; k < 4; ++k) mstar = fmaxf(mstar, mv[k]);
+  for (int r = 0; r < kCombineRowsPerWarp; ++r) {
+    m[r] = -INFINITY;
+    l[r] = 0.f;
+    acc[r] = make_float4(0.f, 0.f, 0.f, 0.f);
   }
-  float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
-  float lstar = 0.f;
-  for (int i0 = 0; i0 < np; i0 += 4) {
-    float mv[4], lv[4];
-    float4 ov[4];
+  for (int g = 0; g < np; g += 4) {
+    float pm[4][kCombineRowsPerWarp], pl[4][kCombineRowsPerWarp];
+    float4 pv[4][kCombineRowsPerWarp];
 #pragma unroll
     for (int k = 0; k < 4; ++k) {
-      if (i0 + k < np) {
-        const float* sl = p.ws + s_slot[i0 + k] * kSlotFloats;
-        mv[k] = sl[kM + row_u];
-        lv[k] = sl[kM + kSlotRows + row_u];
-        ov[k] = *reinterpret_cast<const float4*>(sl + row_u * kHeadDim + lane * 4);
-      } else {
-        mv[k] = -INFINITY;
-        lv[k] = 0.f;
-        ov[k] = make_float4(0.f, 0.f, 0.f, 0.f);
+      const bool have = g + k < np;
+      const float* sl = p.ws + static_cast<long long>(piece_slot(c_lo, slot_lo, c_lo + g + k)) *
+                                   kSlotFloats;
+#pragma unroll
+      for (int r = 0; r < kCombineRowsPerWarp; ++r) {
+        pm[k][r] = have ? __ldg(sl + kM + row0 + r) : -INFINITY;
+        pl[k][r] = have ? __ldg(sl + kM + kSlotRows + row0 + r) : 0.f;
+        pv[k][r] = have ? __ldg(reinterpret_cast<const float4*>(sl + (row0 + r) * kHeadDim) + lane)
+                        : make_float4(0.f, 0.f, 0.f, 0.f);
       }
     }
 #pragma unroll
-    for (int k = 0; k < 4; ++k) {
-      const float w = exp2f(mv[k] - mstar);
-      lstar += w * lv[k];
-      acc.x += w * ov[k].x;
-      acc.y += w * ov[k].y;
-      acc.z += w * ov[k].z;
-      acc.w += w * ov[k].w;
+    for (int r = 0; r < kCombineRowsPerWarp; ++r) {
+      const float mn = fmaxf(fmaxf(m[r], fmaxf(pm[0][r], pm[1][r])), fmaxf(pm[2][r], pm[3][r]));
+      const float sc = ptx::ex2_mufu(m[r] - mn);  // 0 on the first group (m = -inf)
+      l[r] *= sc;
+      acc[r].x *= sc;
+      acc[r].y *= sc;
+      acc[r].z *= sc;
+      acc[r].w *= sc;
+#pragma unroll
+      for (int k = 0; k < 4; ++k) {
+        const float w = ptx::ex2_mufu(pm[k][r] - mn);  // 0 for absent pieces
+        l[r] += w * pl[k][r];
+        acc[r].x += w * pv[k][r].x;
+        acc[r].y += w * pv[k][r].y;
+        acc[r].z += w * pv[k][r].z;
+        acc[r].w += w * pv[k][r].w;
+      }
+      m[r] = mn;
     }
   }
-  const float inv = 1.f / lstar;
-  uint2 pk;
-  pk.x = ptx::bf16x2_pack(acc.x * inv, acc.y * inv);
-  pk.y = ptx::bf16x2_pack(acc.z * inv, acc.w * inv);
-  *reinterpret_cast<uint2*>(p.o + b * p.o_sb + srow * p.o_ss + h * p.o_sh + lane * 4) = pk;
+  const int bh = u / p.n_qblk;
+  const int qb = u - bh * p.n_qblk;
+  const int b = bh / p.H, h = bh - (bh / p.H) * p.H;
+#pragma unroll
+  for (int r = 0; r < kCombineRowsPerWarp; ++r) {
+    const int srow = qb * kUnitRows + row0 + r;
+    if (srow >= p.Sq) break;
+    const float inv = 1.f / l[r];
+    uint2 pk;
+    pk.x = ptx::bf16x2_pack(acc[r].x * inv, acc[r].y * inv);
+    pk.y = ptx::bf16x2_pack(acc[r].z * inv, acc[r].w * inv);
+    *reinterpret_cast<uint2*>(p.o + b * p.o_sb + srow * p.o_ss + h * p.o_sh + lane * 4) = pk;
+  }
 }
 
 }  // namespace llmfa

@@ -167,14 +167,31 @@ Plan make_plan(int n_units, int n_kv, int G, bool have_workspace) {
   const long long sk_total = static_cast<long long>(n_units - dp_units) * n_kv;
   long long parts = sk_total / 4;  // at least 4 KV tiles per piece
   if (parts > G) parts = G;
-  if (parts > llmfa::kCombineMaxPieces) parts = llmfa::kCombineMaxPieces;
-  if (parts < 2) return pl;
+  if (parts < 2 || n_units - dp_units > llmfa::kCombineMaxUnits) return pl;
   pl.sk_mode = 1;
   pl.dp_units = dp_units;
   pl.sk_clusters = static_cast<int>(parts);
   pl.sk_total = sk_total;
   pl.nclusters = dp_units > 0 ? G : pl.sk_clusters;
   return pl;
+}
+
+// The units of a stream-K launch that were cut across clusters, with their
+// pieces, in the combine kernel's table; returns how many.
+int list_split_units(const llmfa::FwdParams& p, llmfa::CombineParams* cp) {
+  int n = 0;
+  for (int u = p.dp_units; u < p.n_units; ++u) {
+    const llmfa::UnitPieces pc = llmfa::unit_pieces(p, u);
+    if (pc.c_lo == pc.c_hi) continue;  // one cluster computed the whole unit
+    if (cp != nullptr) {
+      cp->unit[n] = u;
+      cp->c_lo[n] = static_cast<short>(pc.c_lo);
+      cp->np[n] = static_cast<short>(pc.c_hi - pc.c_lo + 1);
+      cp->slot_lo[n] = static_cast<short>(pc.slot_lo);
+    }
+    ++n;
+  }
+  return n;
 }
 
 __global__ void llmfa_wait_selftest_kernel(unsigned long long timeout_ns, int* status) {
@@ -303,14 +320,28 @@ int llmfa_forward(const void* q, const int64_t q_strides[3], const void* k,
     cp.o_sh = o_strides[2];
     cp.H = p.H;
     cp.Sq = p.Sq;
-    cp.n_kv = p.n_kv;
     cp.n_qblk = p.n_qblk;
-    cp.dp_units = p.dp_units;
-    cp.sk_clusters = p.sk_clusters;
-    cp.sk_total = p.sk_total;
-    const int blocks = (p.n_units - p.dp_units) * (llmfa::kUnitRows / llmfa::kCombineRowsPerCta);
-    llmfa::llm_fa_combine_kernel<<<blocks, 256, 0, st>>>(cp);
-    if (cudaGetLastError() != cudaSuccess) return LLMFA_ERR_LAUNCH;
+    cp.n_split = list_split_units(p, &cp);
+    if (cp.n_split > 0) {
+      constexpr int kWarpsPerUnit = llmfa::kUnitRows / llmfa::kCombineRowsPerWarp;
+      cudaLaunchConfig_t cfg{};
+      cfg.gridDim = dim3((cp.n_split * kWarpsPerUnit + llmfa::kCombineWarpsPerCta - 1) /
+                         llmfa::kCombineWarpsPerCta);
+      cfg.blockDim = dim3(llmfa::kCombineWarpsPerCta * 32);
+      cfg.stream = st;
+      // Programmatic dependent launch: the combine grid is scheduled while the
+      // attention kernel's last CTAs finish and waits (griddepcontrol.wait)
+      // for that kernel's completion before reading the partial results.
+      cudaLaunchAttribute attr{};
+      attr.id = cudaLaunchAttributeProgrammaticStreamSerialization;
+      attr.val.programmaticStreamSerializationAllowed = 1;
+      cfg.attrs = &attr;
+      cfg.numAttrs = 1;
+      if (cudaLaunchKernelEx(&cfg, llmfa::llm_fa_combine_kernel, cp) != cudaSuccess) {
+        cudaGetLastError();
+        return LLMFA_ERR_LAUNCH;
+      }
+    }
   }
   return LLMFA_OK;
 }
@@ -367,9 +398,20 @@ int llmfa_launch_plan(int64_t batch, int64_t heads, int64_t seq_q, int64_t seq_k
   const int G = s->max_clusters;
   const Plan pl =
       make_plan(n_units, n_kv, G, workspace_bytes >= static_cast<uint64_t>(2 * G) * llmfa::kSlotBytes);
-  *kernels = pl.sk_mode ? 2 : 1;
+  int n_split = 0;
+  if (pl.sk_mode) {
+    llmfa::FwdParams p{};
+    p.n_units = n_units;
+    p.n_kv = n_kv;
+    p.sk_mode = 1;
+    p.dp_units = pl.dp_units;
+    p.sk_clusters = pl.sk_clusters;
+    p.sk_total = pl.sk_total;
+    n_split = list_split_units(p, nullptr);
+  }
+  *kernels = n_split > 0 ? 2 : 1;
   *clusters = pl.nclusters;
-  *split_units = pl.sk_mode ? n_units - pl.dp_units : 0;
+  *split_units = n_split;
   return LLMFA_OK;
 }
 

@@ -1,9 +1,10 @@
 // Host-side check of the work split used by the attention kernel (SegIter,
-// sk_owner, combine_slot from fa_fwd_kernel.cuh, compiled here as host code):
-// for many (units, KV tiles, clusters) it checks that every (unit, KV tile)
-// iteration is processed exactly once, that pieces of split units get
-// distinct partial-result slots, and that the combine kernel's slot lookup
-// finds exactly the pieces the kernel wrote. Prints "ok" and exits 0 on success.
+// sk_owner, unit_pieces, piece_slot from fa_fwd_kernel.cuh, compiled here as
+// host code): for many (units, KV tiles, clusters) it checks that every
+// (unit, KV tile) iteration is processed exactly once, that pieces of split
+// units get distinct partial-result slots, and that the combine kernel's slot
+// lookup finds exactly the pieces the kernel wrote. Prints "ok" and exits 0 on
+// success.
 #include <cstdio>
 #include <map>
 #include <set>
@@ -48,21 +49,21 @@ static int check(int n_units, int n_kv, int G, bool sk) {
   for (int v : seen)
     if (v != 1) return 4;
   if (sk) {
-    llmfa::CombineParams cp{};
-    cp.n_kv = n_kv;
-    cp.dp_units = p.dp_units;
-    cp.sk_clusters = p.sk_clusters;
-    cp.sk_total = p.sk_total;
     const long long base = static_cast<long long>(p.dp_units) * n_kv;
+    int n_split = 0;
     for (int u = p.dp_units; u < n_units; ++u) {
       const long long lo = static_cast<long long>(u) * n_kv - base;
-      const int c_lo = llmfa::sk_owner(cp.sk_total, cp.sk_clusters, lo);
-      const int c_hi = llmfa::sk_owner(cp.sk_total, cp.sk_clusters, lo + n_kv - 1);
+      const llmfa::UnitPieces pc = llmfa::unit_pieces(p, u);
+      if (pc.c_lo != llmfa::sk_owner(p.sk_total, p.sk_clusters, lo)) return 6;
       std::set<int> found;
-      if (c_lo != c_hi)
-        for (int c = c_lo; c <= c_hi; ++c) found.insert(llmfa::combine_slot(cp, c, u, base));
+      if (pc.c_lo != pc.c_hi) {
+        ++n_split;
+        for (int c = pc.c_lo; c <= pc.c_hi; ++c) found.insert(llmfa::piece_slot(pc.c_lo, pc.slot_lo, c));
+      }
       if (found != written[u]) return 5;
+      if (pc.c_hi - pc.c_lo + 1 > 32767 || pc.slot_lo > 32767) return 7;  // short fields of the table
     }
+    if (n_split > llmfa::kCombineMaxUnits) return 8;
   }
   return 0;
 }
