@@ -108,8 +108,10 @@ int llmfa_version(void);
 /*
  * Event trace of the last launch (library built with -DLLMFA_TRACE=1 only;
  * otherwise returns LLMFA_ERR_UNSUPPORTED): copies the trace records
- * ({uint64 globaltimer_ns, int64 clock64} per [cta rank][event][iteration])
- * to host memory after synchronising the device. Replaces the reference's
+ * ({uint64 globaltimer_ns, int64 clock64} per [cta rank][Q tile][event]
+ * [iteration]) to host memory after synchronising the device, followed, when
+ * `capacity_bytes` allows, by the per-cluster segment timeline (uint64
+ * [160 clusters][4 segments][4]). Replaces the reference's
  * profiler ring flush (profiler.cuh:85-108) and the prof_buf / prof_count
  * outputs of llm_fa_forward (llm_fa.cu:1461-1474).
  */
@@ -120,7 +122,7 @@ int llmfa_trace_read(void* dst_host, uint64_t capacity_bytes, uint64_t* written_
  * callers that cannot allocate device memory themselves (a foreign-language
  * host that only holds device pointers handed to it, or a framework that
  * plans all device memory up front and forbids allocation on the request
- * path). The split-KV scratch comes from a fixed 39.4 MB array inside this
+ * path). The split-KV scratch comes from a fixed 20.0 MB array inside this
  * library (148 partial-result slots: two per 2-SM cluster of a 148-SM B200),
  * which every GPU that loads the library keeps until the process exits.
  * Returns LLMFA_ERR_UNSUPPORTED on a device that would need more slots than

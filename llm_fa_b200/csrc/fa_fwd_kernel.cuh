@@ -177,7 +177,19 @@ __device__ __forceinline__ void trace_event(int ev, int tile, int j, uint32_t ra
   }
 }
 #define LLMFA_TRACE_EVENT(ev, tile, j) trace_event((ev), (tile), (j), rank, cluster, u)
+// Segment timeline of every cluster (leader CTA): per segment, %globaltimer
+// when the MMA warp issues its first QK, when the epilogue sees O complete
+// (Q tile 0), when the epilogue has written Q tile 1, and u * 65536 + len.
+constexpr int kSegTraceClusters = 160;
+constexpr int kSegTraceSegs = 4;
+__device__ unsigned long long g_seg_trace[kSegTraceClusters * kSegTraceSegs * 4];
+__device__ __forceinline__ void seg_trace(int cluster, int seg, int field, unsigned long long v) {
+  if (cluster < kSegTraceClusters && seg < kSegTraceSegs)
+    g_seg_trace[(cluster * kSegTraceSegs + seg) * 4 + field] = v;
+}
+#define LLMFA_SEG_TRACE(seg, field, v) seg_trace(cluster, (seg), (field), (v))
 #else
+#define LLMFA_SEG_TRACE(seg, field, v) ((void)0)
 #define LLMFA_TRACE_EVENT(ev, tile, j) ((void)0)
 #endif
 
@@ -211,14 +223,18 @@ struct FwdParams {
   int dp_units;
   int sk_clusters;
   long long sk_total;
-  float* ws;         // partial-result slots (sk_mode only)
+  float* ws_ml;      // row max m and row sum l of every partial-result slot (sk_mode only)
 };
 
-// Partial-result slot of a unit split across clusters: unnormalised O
-// (512 rows x 128, fp32), then the row max m (log2 units) and row sum l.
+// Partial-result slot of a unit split across clusters: the piece's O
+// normalised by its own row sum (512 rows x 128, bf16, written by TMA like
+// the final O), and its row max m (log2 units) and row sum l (fp32). A
+// workspace holds the O parts of all slots first, as one [slots*512, 128]
+// bf16 matrix, then [slots][m 512, l 512] fp32.
 constexpr int kSlotRows = kUnitRows;
-constexpr long long kSlotFloats = static_cast<long long>(kSlotRows) * kHeadDim + 2 * kSlotRows;
-constexpr long long kSlotBytes = kSlotFloats * 4;
+constexpr long long kSlotOBytes = static_cast<long long>(kSlotRows) * kHeadDim * 2;
+constexpr long long kSlotMLFloats = 2 * kSlotRows;
+constexpr long long kSlotBytes = kSlotOBytes + kSlotMLFloats * 4;
 
 // Slow path of a bounded wait. With honor_abort, returns early once another
 // role of this CTA has given up.
@@ -368,6 +384,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
                         const __grid_constant__ CUtensorMap tmK,
                         const __grid_constant__ CUtensorMap tmV,
                         const __grid_constant__ CUtensorMap tmO,
+                        const __grid_constant__ CUtensorMap tmW,
                         const __grid_constant__ FwdParams p) {
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   const uint32_t smem_base = (ptx::smem_u32(smem_raw) + 1023u) & ~1023u;
@@ -420,6 +437,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
     ptx::prefetch_tmap(&tmK);
     ptx::prefetch_tmap(&tmV);
     ptx::prefetch_tmap(&tmO);
+    if (p.sk_mode) ptx::prefetch_tmap(&tmW);
   }
   ptx::tc_fence_before();
   __syncthreads();
@@ -624,34 +642,24 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
           break;
         }
         ptx::tc_fence_after();
-        const uint32_t t_o = tmem_base + lane_off + 256 + tile * 128;
-        if (sg.slot >= 0) {
-          // Piece of a unit split across clusters: unnormalised O, m and l to
-          // the partial-result slot; llm_fa_combine_kernel finishes the unit.
-          const int row_u = tile * (kBlockM * kPair) + static_cast<int>(rank) * kBlockM + row;
-          float* slot = p.ws + static_cast<long long>(sg.slot) * kSlotFloats;
-          float* orow_ptr = slot + static_cast<long long>(row_u) * kHeadDim;
-#pragma unroll 1
-          for (int c = 0; c < 4; ++c) {
-            uint32_t r[32];
-            ptx::tmem_ld32(t_o + 32 * c, r);
-            ptx::tmem_wait_ld();
-            ptx::reg_fence32(r);
-#pragma unroll
-            for (int q = 0; q < 8; ++q)
-              *reinterpret_cast<uint4*>(orow_ptr + 32 * c + 4 * q) =
-                  make_uint4(r[4 * q], r[4 * q + 1], r[4 * q + 2], r[4 * q + 3]);
-          }
-          slot[kSlotRows * kHeadDim + row_u] = sm_mrow[(sp * kQTiles + tile) * kBlockM + row];
-          slot[kSlotRows * kHeadDim + kSlotRows + row_u] =
-              sm_lsum[(sp * kQTiles + tile) * kBlockM + row];
-          ptx::tc_fence_before();
-          __syncwarp();
-          if (lane == 0 && has_next)
-            ptx::mbar_arrive_cluster(ptx::mapa(bar(kBarPHalf + tile), 0));
-          continue;  // the staging buffer was not used: its barriers keep their phase
+        if (warp == 8 && lane == 0 && rank == 0 && tile == 0) {
+          LLMFA_SEG_TRACE(static_cast<int>(seg_count), 1, ptx::globaltimer_ns());
+          LLMFA_SEG_TRACE(static_cast<int>(seg_count), 3,
+                          static_cast<unsigned long long>(u) * 65536ull + sg.len);
         }
-        const float inv_l = __frcp_rn(sm_lsum[(sp * kQTiles + tile) * kBlockM + row]);
+        const uint32_t t_o = tmem_base + lane_off + 256 + tile * 128;
+        // O / l in bf16 through the swizzled staging buffer and a TMA store: to
+        // O for a whole unit, to the unit's partial-result slot (with m and l)
+        // for a piece of a unit split across clusters (llm_fa_combine_kernel
+        // merges the pieces).
+        const float lsum = sm_lsum[(sp * kQTiles + tile) * kBlockM + row];
+        const float inv_l = __frcp_rn(lsum);
+        const int row_blk = tile * (kBlockM * kPair) + static_cast<int>(rank) * kBlockM;
+        if (sg.slot >= 0) {
+          float* ml = p.ws_ml + static_cast<long long>(sg.slot) * kSlotMLFloats;
+          ml[row_blk + row] = sm_mrow[(sp * kQTiles + tile) * kBlockM + row];
+          ml[kSlotRows + row_blk + row] = lsum;
+        }
 #pragma unroll 1
         for (int c = 0; c < 4; ++c) {
           uint32_t r[32];
@@ -686,9 +694,12 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
         if (warp == 8 && lane == 0) {
           stored = mbar_wait(bar(kBarOStageFull), stage_phase, wc, kSiteEpiStage) ? 1 : 0;
           if (stored) {
-            const int orow = uc.row0 + tile * (kBlockM * kPair) + static_cast<int>(rank) * kBlockM;
-            ptx::tma_store_4d(&tmO, sO, 0, uc.h, orow, uc.b);
-            ptx::tma_store_4d(&tmO, sO + kPanelBytes, 64, uc.h, orow, uc.b);
+            const bool split = sg.slot >= 0;
+            const CUtensorMap* tm = split ? &tmW : &tmO;
+            const int srow = split ? sg.slot * kSlotRows + row_blk : uc.row0 + row_blk;
+            const int sh = split ? 0 : uc.h, sb = split ? 0 : uc.b;
+            ptx::tma_store_4d(tm, sO, 0, sh, srow, sb);
+            ptx::tma_store_4d(tm, sO + kPanelBytes, 64, sh, srow, sb);
             ptx::bulk_commit_group();
             ptx::bulk_wait_group_read0();
             ptx::mbar_arrive(bar(kBarOStageEmpty));
@@ -701,6 +712,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
           break;
         }
       }
+      if (warp == 8 && lane == 0 && rank == 0)
+        LLMFA_SEG_TRACE(static_cast<int>(seg_count), 2, ptx::globaltimer_ns());
       ++seg_count;
       o_phase ^= 1u;
     }
@@ -786,6 +799,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
           break;
         }
         ptx::tc_fence_after();
+        LLMFA_SEG_TRACE(static_cast<int>(q_use), 0, ptx::globaltimer_ns());
         qk(0, sk);
         commit_both(kBarSFull + 0);
         if (!mbar_wait_warp(bar_local + 8u * (kBarQFull + 1), q_use & 1u, wc, kSiteMmaQFull)) {
@@ -1011,8 +1025,9 @@ __host__ __device__ __forceinline__ int piece_slot(int c_lo, int slot_lo, int c)
 }
 
 // Finishes the units that stream-K mode cut across clusters: for every query
-// row, O = sum_p 2^(m_p - m) O_p / sum_p 2^(m_p - m) l_p over the pieces p
-// (m = max_p m_p), the standard merge of partial softmax states. The host
+// row, O = sum_p w_p O_p / sum_p w_p with w_p = l_p 2^(m_p - m) over the
+// pieces p (O_p normalised by l_p, m = max_p m_p), the standard merge of
+// partial softmax states. The host
 // lists the split units and their pieces. A warp merges 4 rows, one float4
 // column group per lane (coalesced 512-byte rows); the loads of up to four
 // pieces are issued together, and more pieces are folded in groups of four
@@ -1021,7 +1036,8 @@ constexpr int kCombineMaxUnits = 160;  // > clusters of any B200 grid (split uni
 constexpr int kCombineRowsPerWarp = 4;
 constexpr int kCombineWarpsPerCta = 8;
 struct CombineParams {
-  const float* ws;
+  const uint16_t* ws_o;         // [slots * 512, 128] bf16 normalised partial O
+  const float* ws_ml;           // [slots][m 512, l 512]
   uint16_t* o;                  // bf16 output, [B, Sq, H, 128] element strides below
   long long o_sb, o_ss, o_sh;
   int H, Sq, n_qblk, n_split;
@@ -1042,48 +1058,48 @@ __global__ void __launch_bounds__(kCombineWarpsPerCta * 32)
   const int u = p.unit[i];
   const int c_lo = p.c_lo[i], np = p.np[i], slot_lo = p.slot_lo[i];
   const int row0 = (gw - i * kWarpsPerUnit) * kCombineRowsPerWarp;
-  constexpr long long kM = static_cast<long long>(kSlotRows) * kHeadDim;
-  float m[kCombineRowsPerWarp], l[kCombineRowsPerWarp];
+  float m[kCombineRowsPerWarp], wsum[kCombineRowsPerWarp];
   float4 acc[kCombineRowsPerWarp];
 #pragma unroll
   for (int r = 0; r < kCombineRowsPerWarp; ++r) {
     m[r] = -INFINITY;
-    l[r] = 0.f;
+    wsum[r] = 0.f;
     acc[r] = make_float4(0.f, 0.f, 0.f, 0.f);
   }
   for (int g = 0; g < np; g += 4) {
     float pm[4][kCombineRowsPerWarp], pl[4][kCombineRowsPerWarp];
-    float4 pv[4][kCombineRowsPerWarp];
+    uint2 pv[4][kCombineRowsPerWarp];
 #pragma unroll
     for (int k = 0; k < 4; ++k) {
       const bool have = g + k < np;
-      const float* sl = p.ws + static_cast<long long>(piece_slot(c_lo, slot_lo, c_lo + g + k)) *
-                                   kSlotFloats;
+      const long long slot = piece_slot(c_lo, slot_lo, c_lo + g + k);
+      const float* ml = p.ws_ml + slot * kSlotMLFloats;
+      const uint16_t* so = p.ws_o + slot * (kSlotRows * kHeadDim);
 #pragma unroll
       for (int r = 0; r < kCombineRowsPerWarp; ++r) {
-        pm[k][r] = have ? __ldg(sl + kM + row0 + r) : -INFINITY;
-        pl[k][r] = have ? __ldg(sl + kM + kSlotRows + row0 + r) : 0.f;
-        pv[k][r] = have ? __ldg(reinterpret_cast<const float4*>(sl + (row0 + r) * kHeadDim) + lane)
-                        : make_float4(0.f, 0.f, 0.f, 0.f);
+        pm[k][r] = have ? __ldg(ml + row0 + r) : -INFINITY;
+        pl[k][r] = have ? __ldg(ml + kSlotRows + row0 + r) : 0.f;
+        pv[k][r] = have ? __ldg(reinterpret_cast<const uint2*>(so + (row0 + r) * kHeadDim) + lane)
+                        : make_uint2(0u, 0u);
       }
     }
 #pragma unroll
     for (int r = 0; r < kCombineRowsPerWarp; ++r) {
       const float mn = fmaxf(fmaxf(m[r], fmaxf(pm[0][r], pm[1][r])), fmaxf(pm[2][r], pm[3][r]));
       const float sc = ptx::ex2_mufu(m[r] - mn);  // 0 on the first group (m = -inf)
-      l[r] *= sc;
+      wsum[r] *= sc;
       acc[r].x *= sc;
       acc[r].y *= sc;
       acc[r].z *= sc;
       acc[r].w *= sc;
 #pragma unroll
       for (int k = 0; k < 4; ++k) {
-        const float w = ptx::ex2_mufu(pm[k][r] - mn);  // 0 for absent pieces
-        l[r] += w * pl[k][r];
-        acc[r].x += w * pv[k][r].x;
-        acc[r].y += w * pv[k][r].y;
-        acc[r].z += w * pv[k][r].z;
-        acc[r].w += w * pv[k][r].w;
+        const float w = pl[k][r] * ptx::ex2_mufu(pm[k][r] - mn);  // 0 for absent pieces
+        wsum[r] += w;
+        acc[r].x += w * __uint_as_float(pv[k][r].x << 16);
+        acc[r].y += w * __uint_as_float(pv[k][r].x & 0xFFFF0000u);
+        acc[r].z += w * __uint_as_float(pv[k][r].y << 16);
+        acc[r].w += w * __uint_as_float(pv[k][r].y & 0xFFFF0000u);
       }
       m[r] = mn;
     }
@@ -1095,7 +1111,7 @@ __global__ void __launch_bounds__(kCombineWarpsPerCta * 32)
   for (int r = 0; r < kCombineRowsPerWarp; ++r) {
     const int srow = qb * kUnitRows + row0 + r;
     if (srow >= p.Sq) break;
-    const float inv = 1.f / l[r];
+    const float inv = 1.f / wsum[r];
     uint2 pk;
     pk.x = ptx::bf16x2_pack(acc[r].x * inv, acc[r].y * inv);
     pk.y = ptx::bf16x2_pack(acc[r].z * inv, acc[r].w * inv);

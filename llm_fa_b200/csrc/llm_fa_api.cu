@@ -271,7 +271,7 @@ int llmfa_forward(const void* q, const int64_t q_strides[3], const void* k,
   DeviceSetup* s = nullptr;
   if ((rc = device_setup(&dev, &s)) != LLMFA_OK) return rc;
 
-  CUtensorMap tq, tk, tv, to;
+  CUtensorMap tq, tk, tv, to, tw;
   if ((rc = encode_bshd(&tq, q, q_strides, seq_q, heads, batch, llmfa::kBlockM)) != LLMFA_OK)
     return rc;
   if ((rc = encode_bshd(&tk, k, k_strides, seq_k, heads, batch, llmfa::kBlockN / llmfa::kPair)) !=
@@ -305,15 +305,24 @@ int llmfa_forward(const void* q, const int64_t q_strides[3], const void* k,
     p.dp_units = pl.dp_units;
     p.sk_clusters = pl.sk_clusters;
     p.sk_total = pl.sk_total;
-    p.ws = static_cast<float*>(workspace);
+    p.ws_ml = reinterpret_cast<float*>(static_cast<char*>(workspace) +
+                                       static_cast<uint64_t>(2 * G) * llmfa::kSlotOBytes);
+    // the O parts of all slots as one [2G * 512, 128] bf16 matrix
+    const int64_t ws_rows = int64_t(2 * G) * llmfa::kSlotRows;
+    const int64_t ws_strides[3] = {ws_rows * 128, 128, 128};
+    if ((rc = encode_bshd(&tw, workspace, ws_strides, ws_rows, 1, 1, llmfa::kBlockM)) != LLMFA_OK)
+      return rc;
+  } else {
+    tw = to;  // not read without split units
   }
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   llmfa::llm_fa_kernel_sm100<<<dim3(2 * nclusters, 1, 1), dim3(llmfa::kThreads, 1, 1),
-                               llmfa::kSmemBytes, st>>>(tq, tk, tv, to, p);
+                               llmfa::kSmemBytes, st>>>(tq, tk, tv, to, tw, p);
   if (cudaGetLastError() != cudaSuccess) return LLMFA_ERR_LAUNCH;
   if (p.sk_mode) {
     llmfa::CombineParams cp{};
-    cp.ws = p.ws;
+    cp.ws_o = static_cast<const uint16_t*>(workspace);
+    cp.ws_ml = p.ws_ml;
     cp.o = static_cast<uint16_t*>(o);
     cp.o_sb = o_strides[0];
     cp.o_ss = o_strides[1];
@@ -430,6 +439,7 @@ int llmfa_trace_read(void* dst_host, uint64_t capacity_bytes, uint64_t* written_
   *written_bytes = 0;
 #if LLMFA_TRACE
   const uint64_t bytes = sizeof(llmfa::TraceRecord) * llmfa::kTraceRecords;
+  const uint64_t seg_bytes = sizeof(llmfa::g_seg_trace);
   if (capacity_bytes < bytes) return LLMFA_ERR_INVALID_ARGUMENT;
   if (cudaDeviceSynchronize() != cudaSuccess ||
       cudaMemcpyFromSymbol(dst_host, llmfa::g_trace, bytes) != cudaSuccess) {
@@ -437,6 +447,14 @@ int llmfa_trace_read(void* dst_host, uint64_t capacity_bytes, uint64_t* written_
     return LLMFA_ERR_CUDA;
   }
   *written_bytes = bytes;
+  if (capacity_bytes >= bytes + seg_bytes) {  // followed by the segment timeline
+    if (cudaMemcpyFromSymbol(static_cast<char*>(dst_host) + bytes, llmfa::g_seg_trace,
+                             seg_bytes) != cudaSuccess) {
+      cudaGetLastError();
+      return LLMFA_ERR_CUDA;
+    }
+    *written_bytes = bytes + seg_bytes;
+  }
   return LLMFA_OK;
 #else
   (void)capacity_bytes;
@@ -465,12 +483,12 @@ int llmfa_selftest_wait_timeout(uint32_t timeout_us, void* stream) {
 // of device memory at start-up and forbids allocations on the request path.
 // They get the split-KV scratch from this fixed array instead of a workspace
 // argument. It is sized for one 148-SM B200 (two partial-result slots per
-// 2-SM cluster, 74 clusters): 148 x 266,240 bytes = 39.4 MB, held by every
+// 2-SM cluster, 74 clusters): 148 x 135,168 bytes = 20.0 MB, held by every
 // GPU that loads this library until the process exits.
 namespace {
 
 constexpr int kStaticScratchSlots = 148;
-static __device__ __align__(256) float g_static_scratch[kStaticScratchSlots * llmfa::kSlotFloats];
+static __device__ __align__(256) float g_static_scratch[kStaticScratchSlots * llmfa::kSlotBytes / 4];
 
 struct StaticScratch {
   std::once_flag once;

@@ -39,6 +39,26 @@ def read_trace() -> np.ndarray:
     return buf.reshape(2, 2, len(EVENTS), TRACE_ITERS)
 
 
+SEG_CLUSTERS = 160
+SEG_SEGMENTS = 4
+
+
+def read_segments() -> np.ndarray:
+    """Segment timeline of every cluster, uint64 [cluster][segment][4]:
+    %globaltimer of the first QK, of the epilogue seeing O complete, of the
+    epilogue done, then u * 65536 + len (all zero for segments not run)."""
+    n_ev = 2 * 2 * len(EVENTS) * TRACE_ITERS * RECORD.itemsize
+    n_seg = SEG_CLUSTERS * SEG_SEGMENTS * 4 * 8
+    buf = np.zeros(n_ev + n_seg, dtype=np.uint8)
+    written = ctypes.c_uint64(0)
+    rc = _lib.lib().llmfa_trace_read(ctypes.c_void_p(buf.ctypes.data), buf.nbytes,
+                                     ctypes.byref(written))
+    _lib.check(rc, "llmfa_trace_read (library built without LLMFA_TRACE=1?)")
+    if written.value < n_ev + n_seg:
+        raise RuntimeError("library trace has no segment timeline")
+    return buf[n_ev:].view(np.uint64).reshape(SEG_CLUSTERS, SEG_SEGMENTS, 4)
+
+
 def clock_ghz(tr: np.ndarray) -> float:
     """SM clock estimated from the trace: slope of %clock64 against %globaltimer."""
     g = tr["globaltimer_ns"].astype(np.float64)
