@@ -208,6 +208,9 @@ __device__ __forceinline__ uint32_t cta_aborted() {
 }
 __device__ __forceinline__ void cta_abort() { *static_cast<volatile uint32_t*>(&g_cta_abort) = 1u; }
 
+constexpr int kMaxSkParts = 160;  // stream-K ranges (<= clusters of the grid)
+constexpr int kSegmentCost = 1;   // a segment switch costs about this many KV tiles
+
 struct FwdParams {
   int B, H, Sq, Sk;
   int n_qblk;        // ceil(Sq / 512)
@@ -223,6 +226,7 @@ struct FwdParams {
   int dp_units;
   int sk_clusters;
   long long sk_total;
+  long long sk_bound[kMaxSkParts + 1];  // range c = [sk_bound[c], sk_bound[c + 1])
   float* ws_ml;      // row max m and row sum l of every partial-result slot (sk_mode only)
 };
 
@@ -282,9 +286,9 @@ __device__ __forceinline__ UnitCoord decode_unit(const FwdParams& p, int u) {
 // schedule, which keeps concurrently running clusters on the same (batch,
 // head) so K/V tiles are shared in L2. In stream-K mode the units of the
 // last, partial wave are flattened into their units * n_kv iterations and cut
-// into contiguous ranges, one per cluster, so every SM has the same amount of
-// work; a unit cut across clusters is finished by llm_fa_combine_kernel from
-// the fp32 partial results (O, row max, row sum) of each piece.
+// into contiguous ranges, one per cluster, of equal cost (plan_sk_bounds);
+// a unit cut across clusters is finished by llm_fa_combine_kernel from the
+// partial results (normalised O, row max, row sum) of each piece.
 struct Segment {
   int u;     // unit
   int j0;    // first KV tile
@@ -292,15 +296,62 @@ struct Segment {
   int slot;  // partial-result slot, or -1 when this cluster computes the whole unit
 };
 
-__host__ __device__ __forceinline__ long long sk_begin(long long total, int parts, int c) {
-  return c >= parts ? total : total * c / parts;
+__host__ __device__ __forceinline__ long long sk_begin(const FwdParams& p, int c) {
+  return c >= p.sk_clusters ? p.sk_total : p.sk_bound[c];
 }
-// Cluster whose stream-K range holds iteration `it` (0 <= it < total).
-__host__ __device__ __forceinline__ int sk_owner(long long total, int parts, long long it) {
-  int c = static_cast<int>((it * parts) / total);
-  while (c + 1 < parts && sk_begin(total, parts, c + 1) <= it) ++c;
-  while (c > 0 && sk_begin(total, parts, c) > it) --c;
-  return c;
+// Cluster whose stream-K range holds iteration `it` (0 <= it < sk_total).
+__host__ __device__ __forceinline__ int sk_owner(const FwdParams& p, long long it) {
+  int lo = 0, hi = p.sk_clusters - 1;  // largest c with sk_bound[c] <= it
+  while (lo < hi) {
+    const int mid = (lo + hi + 1) >> 1;
+    if (p.sk_bound[mid] <= it) lo = mid;
+    else hi = mid - 1;
+  }
+  return lo;
+}
+
+// Host planner of the stream-K ranges: cuts sk_total iterations into at most
+// `parts` contiguous non-empty ranges. A range costs its KV tiles plus
+// kSegmentCost for every unit boundary inside it (the pipeline drain and
+// refill of a segment switch). Two cuts are compared by their largest range
+// cost: equal lengths, and cut points where the cumulative cost
+// F(pos) = pos + kSegmentCost * (unit boundaries before pos) reaches
+// (c + 1) / parts of F(sk_total). Sets sk_clusters to the number of ranges.
+inline long long sk_max_cost(const long long* b, int n, int n_kv) {
+  long long worst = 0;
+  for (int c = 0; c < n; ++c) {
+    const long long inside = (b[c + 1] - 1) / n_kv - b[c] / n_kv;
+    const long long cost = b[c + 1] - b[c] + static_cast<long long>(kSegmentCost) * inside;
+    worst = cost > worst ? cost : worst;
+  }
+  return worst;
+}
+inline void plan_sk_bounds(FwdParams& p, int parts, int n_kv) {
+  const long long T = p.sk_total;
+  long long even[kMaxSkParts + 1], bal[kMaxSkParts + 1];
+  for (int c = 0; c <= parts; ++c) even[c] = T * c / parts;
+  auto F = [&](long long pos) -> long long {
+    return pos + static_cast<long long>(kSegmentCost) * ((pos - 1) / n_kv);
+  };
+  const long long FT = F(T);
+  int used = 0;
+  long long prev = 0;
+  for (int c = 1; c <= parts && prev < T; ++c) {
+    const long long target = (FT * c + parts - 1) / parts;  // ceil(FT * c / parts)
+    long long lo = prev + 1, hi = T;  // smallest pos > prev with F(pos) >= target
+    while (lo < hi) {
+      const long long mid = (lo + hi) / 2;
+      if (F(mid) >= target) hi = mid;
+      else lo = mid + 1;
+    }
+    bal[used++] = prev;
+    prev = lo;
+  }
+  bal[used] = T;
+  const bool use_bal = sk_max_cost(bal, used, n_kv) <= sk_max_cost(even, parts, n_kv);
+  p.sk_clusters = use_bal ? used : parts;
+  for (int c = 0; c <= kMaxSkParts; ++c)
+    p.sk_bound[c] = c <= p.sk_clusters ? (use_bal ? bal[c] : even[c]) : T;
 }
 
 struct SegIter {
@@ -311,8 +362,8 @@ struct SegIter {
       : c(cluster), G(nclusters), k(0), it(0), end(0), first_sk(true) {
     if (p.sk_mode) {
       const long long base = static_cast<long long>(p.dp_units) * p.n_kv;
-      it = base + sk_begin(p.sk_total, p.sk_clusters, c);
-      end = base + sk_begin(p.sk_total, p.sk_clusters, c + 1);
+      it = base + sk_begin(p, c);
+      end = base + sk_begin(p, c + 1);
     }
   }
   __host__ __device__ __forceinline__ bool next(const FwdParams& p, Segment& s) {
@@ -1015,9 +1066,9 @@ __host__ __device__ __forceinline__ UnitPieces unit_pieces(const FwdParams& p, i
   const long long base = static_cast<long long>(p.dp_units) * p.n_kv;
   const long long it_lo = static_cast<long long>(u) * p.n_kv - base;
   UnitPieces r;
-  r.c_lo = sk_owner(p.sk_total, p.sk_clusters, it_lo);
-  r.c_hi = sk_owner(p.sk_total, p.sk_clusters, it_lo + p.n_kv - 1);
-  r.slot_lo = 2 * r.c_lo + (sk_begin(p.sk_total, p.sk_clusters, r.c_lo) < it_lo ? 1 : 0);
+  r.c_lo = sk_owner(p, it_lo);
+  r.c_hi = sk_owner(p, it_lo + p.n_kv - 1);
+  r.slot_lo = 2 * r.c_lo + (sk_begin(p, r.c_lo) < it_lo ? 1 : 0);
   return r;
 }
 __host__ __device__ __forceinline__ int piece_slot(int c_lo, int slot_lo, int c) {

@@ -150,30 +150,31 @@ int encode_bshd(CUtensorMap* m, const void* ptr, const int64_t* st, int64_t seq,
 
 // Launch plan of one forward: classic persistent schedule, or stream-K over
 // the last partial wave of units when a large enough workspace is given and
-// the classic schedule would leave more than 2% of the clusters idle.
-struct Plan {
-  int nclusters;   // grid size in 2-CTA clusters
-  int sk_mode;
-  int dp_units;
-  int sk_clusters;
-  long long sk_total;
-};
-Plan make_plan(int n_units, int n_kv, int G, bool have_workspace) {
-  Plan pl{n_units < G ? n_units : G, 0, 0, 0, 0};
+// the classic schedule would leave more than 2% of the clusters idle. Fills
+// the work-split fields of `p` (n_units, n_kv set) and returns the grid size
+// in 2-CTA clusters.
+int make_plan(llmfa::FwdParams& p, int G, bool have_workspace) {
+  p.sk_mode = 0;
+  const int n_units = p.n_units;
   const int waves = (n_units + G - 1) / G;
   const double classic_eff = static_cast<double>(n_units) / (static_cast<double>(G) * waves);
-  if (!have_workspace || classic_eff >= 0.98) return pl;
+  const int classic = n_units < G ? n_units : G;
+  if (!have_workspace || classic_eff >= 0.98) return classic;
   const int dp_units = (n_units / G) * G;
-  const long long sk_total = static_cast<long long>(n_units - dp_units) * n_kv;
+  const long long sk_total = static_cast<long long>(n_units - dp_units) * p.n_kv;
   long long parts = sk_total / 4;  // at least 4 KV tiles per piece
   if (parts > G) parts = G;
-  if (parts < 2 || n_units - dp_units > llmfa::kCombineMaxUnits) return pl;
-  pl.sk_mode = 1;
-  pl.dp_units = dp_units;
-  pl.sk_clusters = static_cast<int>(parts);
-  pl.sk_total = sk_total;
-  pl.nclusters = dp_units > 0 ? G : pl.sk_clusters;
-  return pl;
+  if (parts > llmfa::kMaxSkParts) parts = llmfa::kMaxSkParts;
+  if (parts < 2 || n_units - dp_units > llmfa::kCombineMaxUnits) return classic;
+  p.sk_mode = 1;
+  p.dp_units = dp_units;
+  p.sk_total = sk_total;
+  llmfa::plan_sk_bounds(p, static_cast<int>(parts), p.n_kv);
+  if (p.sk_clusters < 2) {
+    p.sk_mode = 0;
+    return classic;
+  }
+  return dp_units > 0 ? G : p.sk_clusters;
 }
 
 // The units of a stream-K launch that were cut across clusters, with their
@@ -297,14 +298,9 @@ int llmfa_forward(const void* q, const int64_t q_strides[3], const void* k,
 
   const int G = s->max_clusters;
   const uint64_t need = static_cast<uint64_t>(2 * G) * llmfa::kSlotBytes;
-  const Plan pl = make_plan(p.n_units, p.n_kv, G,
-                            workspace != nullptr && workspace_bytes >= need && aligned16(workspace));
-  const int nclusters = pl.nclusters;
-  if (pl.sk_mode) {
-    p.sk_mode = 1;
-    p.dp_units = pl.dp_units;
-    p.sk_clusters = pl.sk_clusters;
-    p.sk_total = pl.sk_total;
+  const int nclusters =
+      make_plan(p, G, workspace != nullptr && workspace_bytes >= need && aligned16(workspace));
+  if (p.sk_mode) {
     p.ws_ml = reinterpret_cast<float*>(static_cast<char*>(workspace) +
                                        static_cast<uint64_t>(2 * G) * llmfa::kSlotOBytes);
     // the O parts of all slots as one [2G * 512, 128] bf16 matrix
@@ -405,21 +401,14 @@ int llmfa_launch_plan(int64_t batch, int64_t heads, int64_t seq_q, int64_t seq_k
   const int n_units = static_cast<int>(batch * heads * n_qblk);
   const int n_kv = static_cast<int>((seq_k + llmfa::kBlockN - 1) / llmfa::kBlockN);
   const int G = s->max_clusters;
-  const Plan pl =
-      make_plan(n_units, n_kv, G, workspace_bytes >= static_cast<uint64_t>(2 * G) * llmfa::kSlotBytes);
-  int n_split = 0;
-  if (pl.sk_mode) {
-    llmfa::FwdParams p{};
-    p.n_units = n_units;
-    p.n_kv = n_kv;
-    p.sk_mode = 1;
-    p.dp_units = pl.dp_units;
-    p.sk_clusters = pl.sk_clusters;
-    p.sk_total = pl.sk_total;
-    n_split = list_split_units(p, nullptr);
-  }
+  llmfa::FwdParams p{};
+  p.n_units = n_units;
+  p.n_kv = n_kv;
+  const int nclusters =
+      make_plan(p, G, workspace_bytes >= static_cast<uint64_t>(2 * G) * llmfa::kSlotBytes);
+  const int n_split = p.sk_mode ? list_split_units(p, nullptr) : 0;
   *kernels = n_split > 0 ? 2 : 1;
-  *clusters = pl.nclusters;
+  *clusters = nclusters;
   *split_units = n_split;
   return LLMFA_OK;
 }

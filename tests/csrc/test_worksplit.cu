@@ -25,8 +25,11 @@ static int check(int n_units, int n_kv, int G, bool sk) {
     if (parts < 2) return 0;  // the host would not choose stream-K
     p.sk_mode = 1;
     p.dp_units = dp;
-    p.sk_clusters = static_cast<int>(parts);
     p.sk_total = total;
+    llmfa::plan_sk_bounds(p, static_cast<int>(parts), n_kv);
+    if (p.sk_clusters < 2 || p.sk_clusters > parts) return 9;
+    for (int c = 0; c < p.sk_clusters; ++c)  // non-empty ranges
+      if (p.sk_bound[c + 1] <= p.sk_bound[c] && c + 1 < p.sk_clusters) return 10;
     grid = dp > 0 ? G : p.sk_clusters;
   }
   std::vector<int> seen(static_cast<size_t>(n_units) * n_kv, 0);
@@ -54,7 +57,7 @@ static int check(int n_units, int n_kv, int G, bool sk) {
     for (int u = p.dp_units; u < n_units; ++u) {
       const long long lo = static_cast<long long>(u) * n_kv - base;
       const llmfa::UnitPieces pc = llmfa::unit_pieces(p, u);
-      if (pc.c_lo != llmfa::sk_owner(p.sk_total, p.sk_clusters, lo)) return 6;
+      if (pc.c_lo != llmfa::sk_owner(p, lo)) return 6;
       std::set<int> found;
       if (pc.c_lo != pc.c_hi) {
         ++n_split;
@@ -70,7 +73,7 @@ static int check(int n_units, int n_kv, int G, bool sk) {
 
 int main() {
   int cases = 0;
-  const int Gs[] = {1, 2, 3, 7, 74, 148};
+  const int Gs[] = {1, 2, 3, 7, 74, 148};  // grids above kMaxSkParts are not planned
   for (int G : Gs)
     for (int n_units = 1; n_units <= 600; n_units += (n_units < 40 ? 1 : 37))
       for (int n_kv : {1, 2, 3, 5, 17, 64, 128, 1024})
