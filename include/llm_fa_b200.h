@@ -111,7 +111,7 @@ int llmfa_version(void);
  * ({uint64 globaltimer_ns, int64 clock64} per [cta rank][Q tile][event]
  * [iteration]) to host memory after synchronising the device, followed, when
  * `capacity_bytes` allows, by the per-cluster segment timeline (uint64
- * [160 clusters][4 segments][4]). Replaces the reference's
+ * [160 clusters][32 segments][4]). Replaces the reference's
  * profiler ring flush (profiler.cuh:85-108) and the prof_buf / prof_count
  * outputs of llm_fa_forward (llm_fa.cu:1461-1474).
  */

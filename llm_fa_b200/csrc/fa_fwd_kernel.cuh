@@ -181,7 +181,7 @@ __device__ __forceinline__ void trace_event(int ev, int tile, int j, uint32_t ra
 // when the MMA warp issues its first QK, when the epilogue sees O complete
 // (Q tile 0), when the epilogue has written Q tile 1, and u * 65536 + len.
 constexpr int kSegTraceClusters = 160;
-constexpr int kSegTraceSegs = 4;
+constexpr int kSegTraceSegs = 32;
 __device__ unsigned long long g_seg_trace[kSegTraceClusters * kSegTraceSegs * 4];
 __device__ __forceinline__ void seg_trace(int cluster, int seg, int field, unsigned long long v) {
   if (cluster < kSegTraceClusters && seg < kSegTraceSegs)

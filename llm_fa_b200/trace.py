@@ -40,7 +40,7 @@ def read_trace() -> np.ndarray:
 
 
 SEG_CLUSTERS = 160
-SEG_SEGMENTS = 4
+SEG_SEGMENTS = 32
 
 
 def read_segments() -> np.ndarray:
