@@ -410,7 +410,13 @@ def run_reference(args, cfg, world, rank, local):
                    "timing": f"CUPTI kernel durations of {len(durs)} llm_fa_kernel launches"},
         "kernel_us_per_launch": round(total_us / max(len(durs), 1), 2),
         "gpu_launches": len(durs),
-        "cpu_baseline": cpu,
+        # this run: the reference's own implementation of the path (its llm_fa.cu kernel,
+        # compiled from the reference sources; it has no CPU implementation of the path)
+        "cpu_baseline": {"value": round(value, 2), "unit": UNIT, "cores": 1, "kind": "reference",
+                         "sample": (f"reference llm_fa_kernel (oracle/_ref), {args.steps} steps of "
+                                    f"{len(heads)} launches, whole workload; launched from one "
+                                    "host thread")},
+        "cpu_oracle": cpu,  # the reference's CPU oracle path (fp32 SDPA), for context
         "e2e": {"value": round(value, 2), "unit": UNIT, "h2d_bytes_per_step": 0,
                 "d2h_bytes_per_step": 0},
     })
