@@ -24,7 +24,7 @@
 //
 // Warp roles (16 warps, 512 threads):
 //   0-3  softmax, tile 0          4-7  softmax, tile 1
-//   8-11 correction (O rescale) + epilogue (x 1/l, bf16, TMA store)
+//   8-11 correction (O rescale, exponentials of keys 96-127) + epilogue (x 1/l, bf16, TMA store)
 //   12   MMA issue (leader CTA, whole warp, one elected lane issues) + TMEM allocation
 //   13   TMA producer             14-15 idle
 //
@@ -90,7 +90,10 @@ constexpr uint32_t kSmemScale = kSmemBar + 512;                 // float [2][128
 // waits for that epilogue). float [parity][tile][128] each.
 constexpr uint32_t kSmemLsum = kSmemScale + kQTiles * kBlockM * 4;
 constexpr uint32_t kSmemMrow = kSmemLsum + 2 * kQTiles * kBlockM * 4;
-constexpr uint32_t kSmemTmemSlot = kSmemMrow + 2 * kQTiles * kBlockM * 4;
+// Row max the softmax used for this KV tile's P (the correction warp computes
+// the exponentials of keys 96-127 with it). float [tile][128]
+constexpr uint32_t kSmemMcur = kSmemMrow + 2 * kQTiles * kBlockM * 4;
+constexpr uint32_t kSmemTmemSlot = kSmemMcur + kQTiles * kBlockM * 4;
 constexpr uint32_t kSmemUsed = kSmemTmemSlot + 4;
 constexpr uint32_t kSmemBytes = kSmemUsed + 1024;  // + base-alignment slack
 static_assert(kNumBars * 8 <= 512, "barrier area");
@@ -452,6 +455,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
   float* sm_scale = reinterpret_cast<float*>(smem_gen + kSmemScale);
   float* sm_lsum = reinterpret_cast<float*>(smem_gen + kSmemLsum);
   float* sm_mrow = reinterpret_cast<float*>(smem_gen + kSmemMrow);
+  float* sm_mcur = reinterpret_cast<float*>(smem_gen + kSmemMcur);
   const WaitCtl& wc = p.wait;
 
   // ------------------------------------------------------------ prologue
@@ -461,7 +465,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
       ptx::mbar_init(bar(kBarQEmpty + t), 1);
       ptx::mbar_init(bar(kBarSFull + t), 1);
       ptx::mbar_init(bar(kBarPHalf + t), 16);  // 4 softmax + 4 correction warps x 2 CTAs
-      ptx::mbar_init(bar(kBarPFull + t), 8);   // 4 softmax warps x 2 CTAs
+      ptx::mbar_init(bar(kBarPFull + t), 16);  // 4 softmax + 4 correction warps x 2 CTAs
       ptx::mbar_init(bar(kBarOFull + t), 1);
     }
     for (int s = 0; s < kStages; ++s) {
@@ -553,31 +557,33 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
           mt = fmaxf(fmaxf(chunk_max(s0), chunk_max(s1)), fmaxf(chunk_max(s2), chunk_max(s3))) *
                p.scale_log2;
         }
+        float sc = 1.f;
         if (j == 0) {
           m = mt;
-        } else {
-          float sc = 1.f;
-          if (mt > m + kRescaleThreshold) {
-            sc = ptx::ex2_mufu(m - mt);
-            m = mt;
-            l *= sc;
-          }
-          sm_scale[tile * kBlockM + row] = sc;
-          __syncwarp();
-          if (lane == 0) ptx::mbar_arrive(stat_bar);
-          if (quarter == 0 && lane == 0) LLMFA_TRACE_EVENT(kEvStat, tile, j);
+        } else if (mt > m + kRescaleThreshold) {
+          sc = ptx::ex2_mufu(m - mt);
+          m = mt;
+          l *= sc;
         }
+        // rescale factor (for O and the correction warp's row sum) and the max
+        // used for this tile's P, for the correction warp
+        sm_scale[tile * kBlockM + row] = sc;
+        sm_mcur[tile * kBlockM + row] = m;
+        __syncwarp();
+        if (lane == 0) ptx::mbar_arrive(stat_bar);
+        if (quarter == 0 && lane == 0) LLMFA_TRACE_EVENT(kEvStat, tile, j);
         // Pass 2: P = exp2(s * scale*log2e - m) -> bf16 -> TMEM columns [0, 64),
         // published in two halves so the first four PV k-steps (keys 0-63)
-        // overlap the exponentials of keys 64-127.
+        // overlap the exponentials of keys 64-127. This warp computes keys
+        // 0-95; the correction warp on the same scheduler computes keys 96-127
+        // in parallel (its own MUFU instructions fill this warp's gaps) and
+        // keeps their row sum.
         const uint64_t neg_m2 = ptx::f2_pack(-m, -m);
         uint64_t lsum_a = ptx::f2_pack(0.f, 0.f), lsum_b = lsum_a;
         {
           uint32_t s2[32];
           ptx::tmem_ld32(t_s + 64, s2);
           exp_chunk(s0, c2, neg_m2, lsum_a, t_s + 0);
-          uint32_t s3[32];
-          ptx::tmem_ld32(t_s + 96, s3);
           exp_chunk(s1, c2, neg_m2, lsum_b, t_s + 16);
           ptx::tmem_wait_st();
           ptx::tc_fence_before();
@@ -586,13 +592,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
           if (quarter == 0 && lane == 0) LLMFA_TRACE_EVENT(kEvPHalf, tile, j);
           ptx::tmem_wait_ld();
           ptx::reg_fence32(s2);
-          ptx::reg_fence32(s3);
-          if (last_tile) {
-            mask_tail(s2, 64, p.kv_tail);
-            mask_tail(s3, 96, p.kv_tail);
-          }
+          if (last_tile) mask_tail(s2, 64, p.kv_tail);
           exp_chunk(s2, c2, neg_m2, lsum_a, t_s + 32);
-          exp_chunk(s3, c2, neg_m2, lsum_b, t_s + 48);
         }
         float l0, l1;
         ptx::f2_unpack(ptx::f2_add(lsum_a, lsum_b), l0, l1);
@@ -623,6 +624,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
     const uint32_t sO = smem_base + kSmemO;
     uint32_t stat_phase = 0;  // bit t: phase parity of the tile-t stat barrier
     uint32_t seg_count = 0, o_phase = 0, stage_phase = 0;
+    const uint64_t c2 = ptx::f2_pack(p.scale_log2, p.scale_log2);
+    float lc0 = 0.f, lc1 = 0.f;  // row sums of keys 96-127 (this warp's exponentials), per tile
     bool ok = true;
     bool first = true;
     SegIter si(p, cluster, nclusters);
@@ -639,7 +642,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
         __syncwarp();
         first = false;
       }
-      for (int j = 1; j < sg.len && ok; ++j) {
+      for (int j = 0; j < sg.len && ok; ++j) {
+        const bool last_tile = (sg.j0 + j == p.n_kv - 1);
 #pragma unroll 1
         for (int tile = 0; tile < 2; ++tile) {
           if (!mbar_wait_warp(bar(kBarStat + tile * 4 + quarter), (stat_phase >> tile) & 1u, wc,
@@ -650,7 +654,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
           stat_phase ^= 1u << tile;
           if (warp == 8 && lane == 0) LLMFA_TRACE_EVENT(kEvCorrStat, tile, j);
           const float sc = sm_scale[tile * kBlockM + row];
-          if (__any_sync(0xffffffffu, sc != 1.f)) {
+          const float mcur = sm_mcur[tile * kBlockM + row];
+          if (j > 0 && __any_sync(0xffffffffu, sc != 1.f)) {
             // O_t is quiescent here: PV_t(j-1) completed before S_t(j) was
             // signalled, and PV_t(j) waits for this warp's arrival below.
             ptx::tc_fence_after();
@@ -673,10 +678,34 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
             }
             ptx::tmem_wait_st();
           }
-          ptx::tc_fence_before();
-          __syncwarp();
-          if (lane == 0) ptx::mbar_arrive_cluster(ptx::mapa(bar(kBarPHalf + tile), 0));
-          if (warp == 8 && lane == 0) LLMFA_TRACE_EVENT(kEvCorrArrive, tile, j);
+          if (j > 0) {  // (j = 0: arrived at the segment's start)
+            ptx::tc_fence_before();
+            __syncwarp();
+            if (lane == 0) ptx::mbar_arrive_cluster(ptx::mapa(bar(kBarPHalf + tile), 0));
+            if (warp == 8 && lane == 0) LLMFA_TRACE_EVENT(kEvCorrArrive, tile, j);
+          }
+          // P for keys 96-127 of this tile (TMEM columns 48-63 of S_t; the
+          // softmax warp wrote columns 0-47 and read every score before the
+          // rescale factor was published).
+          {
+            ptx::tc_fence_after();
+            const uint32_t t_s = tmem_base + lane_off + tile * 128;
+            uint32_t r[32];
+            ptx::tmem_ld32(t_s + 96, r);
+            ptx::tmem_wait_ld();
+            ptx::reg_fence32(r);
+            if (last_tile) mask_tail(r, 96, p.kv_tail);
+            uint64_t ls = ptx::f2_pack(0.f, 0.f);
+            exp_chunk(r, c2, ptx::f2_pack(-mcur, -mcur), ls, t_s + 48);
+            float a, b;
+            ptx::f2_unpack(ls, a, b);
+            if (tile == 0) lc0 = (j == 0 ? 0.f : lc0 * sc) + (a + b);
+            else lc1 = (j == 0 ? 0.f : lc1 * sc) + (a + b);
+            ptx::tmem_wait_st();
+            ptx::tc_fence_before();
+            __syncwarp();
+            if (lane == 0) ptx::mbar_arrive_cluster(ptx::mapa(bar(kBarPFull + tile), 0));
+          }
         }
       }
       if (!ok) break;
@@ -703,7 +732,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
         // O for a whole unit, to the unit's partial-result slot (with m and l)
         // for a piece of a unit split across clusters (llm_fa_combine_kernel
         // merges the pieces).
-        const float lsum = sm_lsum[(sp * kQTiles + tile) * kBlockM + row];
+        const float lsum = sm_lsum[(sp * kQTiles + tile) * kBlockM + row] + (tile == 0 ? lc0 : lc1);
         const float inv_l = __frcp_rn(lsum);
         const int row_blk = tile * (kBlockM * kPair) + static_cast<int>(rank) * kBlockM;
         if (sg.slot >= 0) {
