@@ -19,7 +19,9 @@ C2 = np.float32(float.fromhex("0x1.f0de1ap-3"))
 C3 = np.float32(float.fromhex("0x1.c3f76p-5"))
 MAGIC = np.float32(12582912.0)
 RESCALE_THRESHOLD = np.float32(8.0)
-POLY_MASK = 0x8888  # pairs (within each 32-column chunk) that use the polynomial
+# pairs (within each 32-column chunk) that use the polynomial: the kernel's default
+# (LLMFA_SOFTMAX_POLY_MASK in fa_fwd_kernel.cuh)
+POLY_MASK = 0x8000
 
 
 def bf16_round(x: np.ndarray) -> np.ndarray:
@@ -46,18 +48,21 @@ def exp2_poly(x: np.ndarray) -> np.ndarray:
     return (bits & 0xFFFFFFFF).astype(np.uint32).view(np.float32)
 
 
-def poly_columns() -> np.ndarray:
+def poly_columns(mask: int = POLY_MASK) -> np.ndarray:
     cols = np.zeros(128, dtype=bool)
     for c in range(4):
         for k in range(16):
-            if (POLY_MASK >> k) & 1:
+            if (mask >> k) & 1:
                 cols[32 * c + 2 * k] = cols[32 * c + 2 * k + 1] = True
     return cols
 
 
 def attention_kernel_emulation(q: np.ndarray, k: np.ndarray, v: np.ndarray,
-                               scale: float) -> np.ndarray:
-    """q (Sq,D), k/v (Sk,D) float32 (bf16-valued) -> O (Sq,D) float32 (bf16-valued)."""
+                               scale: float, poly_mask: int = POLY_MASK) -> np.ndarray:
+    """q (Sq,D), k/v (Sk,D) float32 (bf16-valued) -> O (Sq,D) float32 (bf16-valued).
+
+    `poly_mask` selects the column pairs whose exp2 uses the polynomial (0xFFFF
+    sends every column through it, which stresses the polynomial)."""
     q = q.astype(np.float32)
     k = k.astype(np.float32)
     v = v.astype(np.float32)
@@ -67,7 +72,7 @@ def attention_kernel_emulation(q: np.ndarray, k: np.ndarray, v: np.ndarray,
     m = np.zeros(Sq, np.float32)
     l = np.zeros(Sq, np.float32)
     o = np.zeros((Sq, D), np.float32)
-    polyc = poly_columns()
+    polyc = poly_columns(poly_mask)
     n_kv = (Sk + 127) // 128
     for j in range(n_kv):
         kt = k[128 * j:128 * (j + 1)]

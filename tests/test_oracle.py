@@ -85,8 +85,9 @@ def test_exp2_polynomial_error_bound():
     assert np.all(exp2_poly(np.array([-1e30, -np.inf], np.float32)) < 1e-37)
 
 
+@pytest.mark.parametrize("poly_mask", [0x8000, 0xFFFF])
 @pytest.mark.parametrize("name", ["small", "ragged", "stress"])
-def test_kernel_algorithm_emulation_within_tolerance(golden, name):
+def test_kernel_algorithm_emulation_within_tolerance(golden, name, poly_mask):
     cfg, rows = _case(golden, name)
     q, k, v = make_inputs(cfg)
     ref = torch.from_numpy(golden[f"{name}/o"])
@@ -94,7 +95,7 @@ def test_kernel_algorithm_emulation_within_tolerance(golden, name):
     for b in range(cfg.batch):
         for h in range(cfg.heads):
             o = attention_kernel_emulation(q[b, :, h].float().numpy(), k[b, :, h].float().numpy(),
-                                           v[b, :, h].float().numpy(), cfg.scale)
+                                           v[b, :, h].float().numpy(), cfg.scale, poly_mask)
             out[b, :, h] = torch.from_numpy(o[rows.numpy()])
     err = compare(out, ref)
     assert err["max_abs"] < MAX_ABS_TOL and err["mean_abs"] < MEAN_ABS_TOL, err
