@@ -60,6 +60,22 @@ int llmfa_forward(const void* q, const int64_t q_strides[3], const void* k,
                   int64_t seq_k, float softmax_scale, void* workspace, uint64_t workspace_bytes,
                   void* stream);
 
+/*
+ * llmfa_forward that also writes the natural-log log-sum-exp of every query
+ * row's scaled scores, lse[b, h, s] = log(sum_k exp(q_s . k_k * softmax_scale)),
+ * fp32, at lse + b * lse_strides[0] + h * lse_strides[1] + s (rows contiguous;
+ * 4-byte aligned). This is the per-row softmax normaliser that split-KV merges
+ * and a backward pass consume; for query blocks whose KV range is split it
+ * comes from the combine step. lse = NULL behaves as llmfa_forward. No
+ * counterpart in the reference (its launcher returns O only, llm_fa.cu:1475).
+ */
+int llmfa_forward_lse(const void* q, const int64_t q_strides[3], const void* k,
+                      const int64_t k_strides[3], const void* v, const int64_t v_strides[3],
+                      void* o, const int64_t o_strides[3], float* lse,
+                      const int64_t lse_strides[2], int64_t batch, int64_t heads, int64_t seq_q,
+                      int64_t seq_k, float softmax_scale, void* workspace,
+                      uint64_t workspace_bytes, void* stream);
+
 /* Workspace bytes that let llmfa_forward split KV ranges on the current
  * device (depends on the device's SM count only, not on the shapes). No
  * counterpart in the reference, which always launches one cluster per 512

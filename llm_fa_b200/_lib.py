@@ -23,6 +23,7 @@ LLMFA_ERR_DEVICE_TIMEOUT = 6
 DEVICE_STATUS_TIMEOUT_BASE = 0x1000
 
 _I64x3 = ctypes.c_int64 * 3
+_I64x2 = ctypes.c_int64 * 2
 _lock = threading.Lock()
 _lib = None
 
@@ -32,6 +33,12 @@ SIGNATURES = {
         ctypes.c_void_p, _I64x3, ctypes.c_void_p, _I64x3, ctypes.c_void_p, _I64x3,
         ctypes.c_void_p, _I64x3, ctypes.c_int64, ctypes.c_int64, ctypes.c_int64,
         ctypes.c_int64, ctypes.c_float, ctypes.c_void_p, ctypes.c_uint64, ctypes.c_void_p]),
+    "llmfa_forward_lse": (ctypes.c_int, [
+        ctypes.c_void_p, _I64x3, ctypes.c_void_p, _I64x3, ctypes.c_void_p, _I64x3,
+        ctypes.c_void_p, _I64x3, ctypes.c_void_p, ctypes.POINTER(ctypes.c_int64),
+        ctypes.c_int64, ctypes.c_int64,
+        ctypes.c_int64, ctypes.c_int64, ctypes.c_float, ctypes.c_void_p, ctypes.c_uint64,
+        ctypes.c_void_p]),
     "llmfa_workspace_size": (ctypes.c_int, [ctypes.POINTER(ctypes.c_uint64)]),
     "llmfa_forward_static_scratch": (ctypes.c_int, [
         ctypes.c_void_p, _I64x3, ctypes.c_void_p, _I64x3, ctypes.c_void_p, _I64x3,
@@ -94,3 +101,7 @@ def check(code: int, what: str) -> None:
 
 def strides3(st) -> ctypes.Array:
     return _I64x3(*[int(x) for x in st])
+
+
+def strides2(st) -> ctypes.Array:
+    return _I64x2(*[int(x) for x in st])

@@ -42,12 +42,15 @@ def _check(t: torch.Tensor, name: str, device: torch.device) -> None:
 
 def attention_forward(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, *,
                       softmax_scale: float | None = None,
-                      out: torch.Tensor | None = None) -> torch.Tensor:
+                      out: torch.Tensor | None = None, return_lse: bool = False):
     """O = softmax(Q K^T * softmax_scale) V on the current CUDA stream.
 
     softmax_scale defaults to 1/sqrt(128) (the reference's scale,
     validate.py:19-27). `out`, if given, must have Q's shape and be bf16.
-    Raises RuntimeError on invalid input or a nonzero library status.
+    With return_lse, returns (O, lse): the fp32 natural-log log-sum-exp of each
+    query row's scaled scores, shaped [B, H, Sq] for 4-D inputs and [Sq] for
+    2-D ones (llmfa_forward_lse). Raises RuntimeError on invalid input or a
+    nonzero library status.
     """
     device = q.device
     for t, nm in ((q, "Q"), (k, "K"), (v, "V")):
@@ -77,14 +80,19 @@ def attention_forward(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, *,
         ws_bytes = workspace_size(device)
         ws = torch.empty(ws_bytes, dtype=torch.uint8, device=device)
         stream = torch.cuda.current_stream(device).cuda_stream
-        rc = L.llmfa_forward(
+        lse = torch.empty(B, H, Sq, dtype=torch.float32, device=device) if return_lse else None
+        rc = L.llmfa_forward_lse(
             ctypes.c_void_p(q4.data_ptr()), _lib.strides3(q4.stride()[:3]),
             ctypes.c_void_p(k4.data_ptr()), _lib.strides3(k4.stride()[:3]),
             ctypes.c_void_p(v4.data_ptr()), _lib.strides3(v4.stride()[:3]),
             ctypes.c_void_p(o4.data_ptr()), _lib.strides3(o4.stride()[:3]),
+            ctypes.c_void_p(lse.data_ptr() if return_lse else None),
+            _lib.strides2((H * Sq, Sq)),
             B, H, Sq, Sk, ctypes.c_float(scale), ctypes.c_void_p(ws.data_ptr()), ws_bytes,
             ctypes.c_void_p(stream))
-    _lib.check(rc, "llmfa_forward")
+    _lib.check(rc, "llmfa_forward_lse")
+    if return_lse:
+        return out, (lse if q.dim() == 4 else lse.reshape(Sq))
     return out
 
 

@@ -231,6 +231,10 @@ struct FwdParams {
   long long sk_total;
   long long sk_bound[kMaxSkParts + 1];  // range c = [sk_bound[c], sk_bound[c + 1])
   float* ws_ml;      // row max m and row sum l of every partial-result slot (sk_mode only)
+  // Optional natural-log log-sum-exp of every query row's scaled scores,
+  // lse[b * lse_sb + h * lse_sh + row] = log(sum_k exp(s_k * scale)); null = not written.
+  float* lse;
+  long long lse_sb, lse_sh;
 };
 
 // Partial-result slot of a unit split across clusters: the piece's O
@@ -735,6 +739,12 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
         const float lsum = sm_lsum[(sp * kQTiles + tile) * kBlockM + row] + (tile == 0 ? lc0 : lc1);
         const float inv_l = __frcp_rn(lsum);
         const int row_blk = tile * (kBlockM * kPair) + static_cast<int>(rank) * kBlockM;
+        if (p.lse != nullptr && sg.slot < 0 && uc.row0 + row_blk + row < p.Sq) {
+          // sum_k exp(s_k * scale) = 2^m * l with m in log2 units
+          const float m2 = sm_mrow[(sp * kQTiles + tile) * kBlockM + row];
+          p.lse[uc.b * p.lse_sb + uc.h * p.lse_sh + uc.row0 + row_blk + row] =
+              (m2 + __log2f(lsum)) * 0.6931471805599453f;
+        }
         if (sg.slot >= 0) {
           float* ml = p.ws_ml + static_cast<long long>(sg.slot) * kSlotMLFloats;
           ml[row_blk + row] = sm_mrow[(sp * kQTiles + tile) * kBlockM + row];
@@ -1120,6 +1130,8 @@ struct CombineParams {
   const float* ws_ml;           // [slots][m 512, l 512]
   uint16_t* o;                  // bf16 output, [B, Sq, H, 128] element strides below
   long long o_sb, o_ss, o_sh;
+  float* lse;                   // optional log-sum-exp output (see FwdParams)
+  long long lse_sb, lse_sh;
   int H, Sq, n_qblk, n_split;
   int unit[kCombineMaxUnits];   // split units
   short c_lo[kCombineMaxUnits], np[kCombineMaxUnits], slot_lo[kCombineMaxUnits];
@@ -1196,6 +1208,8 @@ __global__ void __launch_bounds__(kCombineWarpsPerCta * 32)
     pk.x = ptx::bf16x2_pack(acc[r].x * inv, acc[r].y * inv);
     pk.y = ptx::bf16x2_pack(acc[r].z * inv, acc[r].w * inv);
     *reinterpret_cast<uint2*>(p.o + b * p.o_sb + srow * p.o_ss + h * p.o_sh + lane * 4) = pk;
+    if (p.lse != nullptr && lane == 0)  // sum = 2^m * sum_p w_p
+      p.lse[b * p.lse_sb + h * p.lse_sh + srow] = (m[r] + __log2f(wsum[r])) * 0.6931471805599453f;
   }
 }
 

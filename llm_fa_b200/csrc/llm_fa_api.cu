@@ -253,6 +253,17 @@ int llmfa_forward(const void* q, const int64_t q_strides[3], const void* k,
                   const int64_t o_strides[3], int64_t batch, int64_t heads, int64_t seq_q,
                   int64_t seq_k, float softmax_scale, void* workspace, uint64_t workspace_bytes,
                   void* stream) {
+  return llmfa_forward_lse(q, q_strides, k, k_strides, v, v_strides, o, o_strides, nullptr,
+                           nullptr, batch, heads, seq_q, seq_k, softmax_scale, workspace,
+                           workspace_bytes, stream);
+}
+
+int llmfa_forward_lse(const void* q, const int64_t q_strides[3], const void* k,
+                      const int64_t k_strides[3], const void* v, const int64_t v_strides[3],
+                      void* o, const int64_t o_strides[3], float* lse,
+                      const int64_t lse_strides[2], int64_t batch, int64_t heads, int64_t seq_q,
+                      int64_t seq_k, float softmax_scale, void* workspace,
+                      uint64_t workspace_bytes, void* stream) {
   // ---- argument checks (no CUDA call before they pass)
   if (batch < 1 || heads < 1 || seq_q < 1 || seq_k < 1) return LLMFA_ERR_INVALID_ARGUMENT;
   if (!(softmax_scale > 0.f) || !std::isfinite(softmax_scale)) return LLMFA_ERR_INVALID_ARGUMENT;
@@ -267,6 +278,12 @@ int llmfa_forward(const void* q, const int64_t q_strides[3], const void* k,
   if ((rc = check_view(k, k_strides, seq_k, heads, batch)) != LLMFA_OK) return rc;
   if ((rc = check_view(v, v_strides, seq_k, heads, batch)) != LLMFA_OK) return rc;
   if ((rc = check_view(o, o_strides, seq_q, heads, batch)) != LLMFA_OK) return rc;
+  if (lse != nullptr) {  // [batch, heads, seq_q] fp32, rows contiguous
+    if (lse_strides == nullptr || (reinterpret_cast<uintptr_t>(lse) & 3u) != 0)
+      return LLMFA_ERR_INVALID_ARGUMENT;
+    if ((batch > 1 && lse_strides[0] < 1) || (heads > 1 && lse_strides[1] < 1))
+      return LLMFA_ERR_INVALID_ARGUMENT;
+  }
 
   int dev = 0;
   DeviceSetup* s = nullptr;
@@ -293,6 +310,9 @@ int llmfa_forward(const void* q, const int64_t q_strides[3], const void* k,
   p.n_units = static_cast<int>(n_units);
   p.kv_tail = static_cast<int>(seq_k - int64_t(p.n_kv - 1) * llmfa::kBlockN);
   p.scale_log2 = softmax_scale * 1.4426950408889634f;
+  p.lse = lse;
+  p.lse_sb = lse != nullptr ? lse_strides[0] : 0;
+  p.lse_sh = lse != nullptr ? lse_strides[1] : 0;
   p.wait.timeout_ns = wait_timeout_ns();
   p.wait.status = s->status_ptr;
 
@@ -323,6 +343,9 @@ int llmfa_forward(const void* q, const int64_t q_strides[3], const void* k,
     cp.o_sb = o_strides[0];
     cp.o_ss = o_strides[1];
     cp.o_sh = o_strides[2];
+    cp.lse = p.lse;
+    cp.lse_sb = p.lse_sb;
+    cp.lse_sh = p.lse_sh;
     cp.H = p.H;
     cp.Sq = p.Sq;
     cp.n_qblk = p.n_qblk;

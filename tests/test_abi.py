@@ -70,6 +70,24 @@ def test_bad_arguments_are_rejected_without_cuda(L, kw, code):
     assert _call(L, **kw) == code
 
 
+def test_lse_entry_point_rejects_bad_lse_arguments_without_cuda(L):
+    ptr = ctypes.c_void_p
+    qs = _lib.strides3((1024 * 128, 128, 128))
+
+    def call(lse, lse_strides, B=1, H=1):
+        return L.llmfa_forward_lse(ptr(16), qs, ptr(16), qs, ptr(16), qs, ptr(16), qs,
+                                   ptr(lse) if lse else None, lse_strides, B, H, 1024, 1024,
+                                   ctypes.c_float(0.088), None, 0, None)
+
+    assert call(64, None) == _lib.LLMFA_ERR_INVALID_ARGUMENT              # no strides
+    assert call(66, _lib.strides2((1024, 1024))) == _lib.LLMFA_ERR_INVALID_ARGUMENT  # misaligned
+    assert call(64, _lib.strides2((0, 1024)), B=2) == _lib.LLMFA_ERR_INVALID_ARGUMENT  # batch stride
+    # the shared argument checks still run first
+    assert L.llmfa_forward_lse(None, qs, ptr(16), qs, ptr(16), qs, ptr(16), qs, None, None, 1, 1,
+                               1024, 1024, ctypes.c_float(0.088), None, 0,
+                               None) == _lib.LLMFA_ERR_INVALID_ARGUMENT
+
+
 def test_small_helpers_validate(L):
     assert L.llmfa_set_wait_timeout_ms(0) == _lib.LLMFA_ERR_INVALID_ARGUMENT
     assert L.llmfa_device_status(None, None) == _lib.LLMFA_ERR_INVALID_ARGUMENT

@@ -233,6 +233,38 @@ def _forward_c_abi(q, k, v, workspace: bool):
     return o.cpu()
 
 
+@pytest.mark.parametrize("B,H,Sq,Sk", [(1, 2, 1000, 2049), (2, 3, 700, 2500), (1, 1, 512, 8192),
+                                        (2, 4, 1024, 1024), (1, 1, 16384, 4096)])
+def test_log_sum_exp_output(B, H, Sq, Sk):
+    """llmfa_forward_lse: per-row log(sum_k exp(s_k * scale)) against fp32 logsumexp on the
+    GPU, for whole and split-KV query blocks; O identical to the plain call."""
+    cfg = Config("lse", B, H, Sq, Sk, seed=Sq + 3 * Sk + H)
+    q, k, v = (t.cuda() for t in make_inputs(cfg))
+    o, lse = attention_forward(q, k, v, return_lse=True)
+    o_plain = attention_forward(q, k, v)
+    torch.cuda.synchronize()
+    assert device_status() == 0
+    assert lse.shape == (B, H, Sq) and lse.dtype == torch.float32
+    assert torch.equal(o, o_plain)
+    prev = torch.backends.cuda.matmul.allow_tf32
+    torch.backends.cuda.matmul.allow_tf32 = False
+    try:
+        qh, kh = q.permute(0, 2, 1, 3).float(), k.permute(0, 2, 1, 3).float()
+        ref = torch.empty(B, H, Sq, device=q.device)
+        for s0 in range(0, Sq, 2048):
+            ref[:, :, s0:s0 + 2048] = torch.logsumexp(
+                qh[:, :, s0:s0 + 2048] @ kh.transpose(-1, -2) * cfg.scale, dim=-1)
+    finally:
+        torch.backends.cuda.matmul.allow_tf32 = prev
+    err = (lse - ref).abs().max().item()
+    assert math.isfinite(err) and err < 1e-3, err
+    # 2-D inputs return [Sq]
+    o2, lse2 = attention_forward(q[0, :, 0].contiguous(), k[0, :, 0].contiguous(),
+                                 v[0, :, 0].contiguous(), return_lse=True)
+    assert lse2.shape == (Sq,)
+    assert (lse2 - ref[0, 0]).abs().max().item() < 1e-3
+
+
 # (1, 1, 2048, 2176): a cluster's one-tile segment follows a multi-tile one, the case
 # where the end-of-segment row sums must not be overwritten before they are read;
 # (2, 64, 1024, 100): many one-tile units per cluster in the round-robin part.
