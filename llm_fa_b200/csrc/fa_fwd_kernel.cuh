@@ -437,6 +437,10 @@ __device__ __forceinline__ void exp_chunk(const uint32_t (&r)[32], uint64_t c2, 
   ptx::tmem_st16(t_p, pk);
 }
 
+// kWithLse: also write the per-row log-sum-exp (FwdParams::lse). A separate
+// instantiation, so the plain forward's code is not touched by it (the
+// correction warps' register allocation moved the plain path by ~3%).
+template <bool kWithLse>
 __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
     llm_fa_kernel_sm100(const __grid_constant__ CUtensorMap tmQ,
                         const __grid_constant__ CUtensorMap tmK,
@@ -739,7 +743,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
         const float lsum = sm_lsum[(sp * kQTiles + tile) * kBlockM + row] + (tile == 0 ? lc0 : lc1);
         const float inv_l = __frcp_rn(lsum);
         const int row_blk = tile * (kBlockM * kPair) + static_cast<int>(rank) * kBlockM;
-        if (p.lse != nullptr && sg.slot < 0 && uc.row0 + row_blk + row < p.Sq) {
+        if (kWithLse && sg.slot < 0 && uc.row0 + row_blk + row < p.Sq) {
           // sum_k exp(s_k * scale) = 2^m * l with m in log2 units
           const float m2 = sm_mrow[(sp * kQTiles + tile) * kBlockM + row];
           p.lse[uc.b * p.lse_sb + uc.h * p.lse_sh + uc.row0 + row_blk + row] =

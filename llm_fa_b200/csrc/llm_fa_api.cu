@@ -78,7 +78,10 @@ int device_setup(int* dev_out, DeviceSetup** out) {
   }
   DeviceSetup& s = g_setup[dev];
   std::call_once(s.once, [&] {
-    if (cudaFuncSetAttribute(llmfa::llm_fa_kernel_sm100,
+    if (cudaFuncSetAttribute(llmfa::llm_fa_kernel_sm100<false>,
+                             cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             static_cast<int>(llmfa::kSmemBytes)) != cudaSuccess ||
+        cudaFuncSetAttribute(llmfa::llm_fa_kernel_sm100<true>,
                              cudaFuncAttributeMaxDynamicSharedMemorySize,
                              static_cast<int>(llmfa::kSmemBytes)) != cudaSuccess) {
       cudaGetLastError();
@@ -97,7 +100,7 @@ int device_setup(int* dev_out, DeviceSetup** out) {
     cfg.gridDim = dim3(2, 1, 1);
     cfg.blockDim = dim3(llmfa::kThreads, 1, 1);
     cfg.dynamicSmemBytes = llmfa::kSmemBytes;
-    if (cudaOccupancyMaxActiveClusters(&n, llmfa::llm_fa_kernel_sm100, &cfg) != cudaSuccess ||
+    if (cudaOccupancyMaxActiveClusters(&n, llmfa::llm_fa_kernel_sm100<false>, &cfg) != cudaSuccess ||
         n <= 0) {
       cudaGetLastError();
       int sms = 0;
@@ -332,8 +335,12 @@ int llmfa_forward_lse(const void* q, const int64_t q_strides[3], const void* k,
     tw = to;  // not read without split units
   }
   cudaStream_t st = static_cast<cudaStream_t>(stream);
-  llmfa::llm_fa_kernel_sm100<<<dim3(2 * nclusters, 1, 1), dim3(llmfa::kThreads, 1, 1),
-                               llmfa::kSmemBytes, st>>>(tq, tk, tv, to, tw, p);
+  if (p.lse != nullptr)
+    llmfa::llm_fa_kernel_sm100<true><<<dim3(2 * nclusters, 1, 1), dim3(llmfa::kThreads, 1, 1),
+                                       llmfa::kSmemBytes, st>>>(tq, tk, tv, to, tw, p);
+  else
+    llmfa::llm_fa_kernel_sm100<false><<<dim3(2 * nclusters, 1, 1), dim3(llmfa::kThreads, 1, 1),
+                                        llmfa::kSmemBytes, st>>>(tq, tk, tv, to, tw, p);
   if (cudaGetLastError() != cudaSuccess) return LLMFA_ERR_LAUNCH;
   if (p.sk_mode) {
     llmfa::CombineParams cp{};
