@@ -45,7 +45,7 @@ PUBLISHED_REF_TFLOPS = {"c2": 362.5, "c3": 810.6}
 # summarised in profiles/; None until measured for that configuration.
 PROFILED_TRAFFIC_BYTES: dict[str, float | None] = {
     "c2": 12.66e6,   # profiles/llm_fa_kernel_c2_ncu.md
-    "c3": 179.3e6,   # profiles/llm_fa_kernel_c3_ncu.md
+    "c3": 142.6e6,   # profiles/llm_fa_kernel_c3_ncu.md
 }
 L2_FLUSH_BYTES = 256 << 20
 
