@@ -112,12 +112,14 @@ static_assert(2 * 128 * kRegsSoftmax + 128 * kRegsCorrection + 128 * kRegsContro
 constexpr float kRescaleThreshold = 8.0f;  // log2 units
 // Pairs (bit k = columns 2k, 2k+1) of each 32-column chunk whose exp2 runs on
 // the FMA pipe (softmax_exp2.cuh) instead of MUFU; the rest use ex2.approx.
-// Default: the last pair of each chunk (1/16 of the exponentials). Measured on
-// B200 against all-MUFU and against 1/8 and 1/4 offloads at several positions,
-// in one process with interleaved runs: +4% (Sq=Sk=16384) and +5.6%
-// (Sq=32768, Sk=131072); larger fractions lose to the extra FMA-pipe issue.
+// Default: pair 7 of each chunk (1/16 of the exponentials). Measured on B200
+// against all-MUFU and against 1/8 and 1/4 offloads at several positions, in
+// one process with interleaved runs: +4% (Sq=Sk=16384) and +5.6% (Sq=32768,
+// Sk=131072) over all-MUFU; pair 7 is a further ~+0.8% over pair 15 since the
+// correction warps took keys 96-127; larger fractions lose to the extra
+// FMA-pipe issue.
 #ifndef LLMFA_SOFTMAX_POLY_MASK
-#define LLMFA_SOFTMAX_POLY_MASK 0x8000u
+#define LLMFA_SOFTMAX_POLY_MASK 0x0080u
 #endif
 constexpr uint32_t kSoftmaxPolyMask = LLMFA_SOFTMAX_POLY_MASK;
 

@@ -21,7 +21,7 @@ MAGIC = np.float32(12582912.0)
 RESCALE_THRESHOLD = np.float32(8.0)
 # pairs (within each 32-column chunk) that use the polynomial: the kernel's default
 # (LLMFA_SOFTMAX_POLY_MASK in fa_fwd_kernel.cuh)
-POLY_MASK = 0x8000
+POLY_MASK = 0x0080
 
 
 def bf16_round(x: np.ndarray) -> np.ndarray:
