@@ -341,22 +341,26 @@ inline void plan_sk_bounds(FwdParams& p, int parts, int n_kv) {
   const long long T = p.sk_total;
   long long even[kMaxSkParts + 1], bal[kMaxSkParts + 1];
   for (int c = 0; c <= parts; ++c) even[c] = T * c / parts;
+  // F takes the values u (n_kv + X) + 1 .. u (n_kv + X) + n_kv on unit u's
+  // positions u n_kv + 1 .. u n_kv + n_kv (X = kSegmentCost) and skips the next
+  // X values, so the smallest pos with F(pos) >= t has a closed form.
+  const long long w = static_cast<long long>(n_kv) + kSegmentCost;
   auto F = [&](long long pos) -> long long {
     return pos + static_cast<long long>(kSegmentCost) * ((pos - 1) / n_kv);
+  };
+  auto F_inverse = [&](long long t) -> long long {
+    const long long u = (t - 1) / w, r = t - u * w;
+    return r <= n_kv ? u * n_kv + r : (u + 1) * n_kv + 1;
   };
   const long long FT = F(T);
   int used = 0;
   long long prev = 0;
   for (int c = 1; c <= parts && prev < T; ++c) {
     const long long target = (FT * c + parts - 1) / parts;  // ceil(FT * c / parts)
-    long long lo = prev + 1, hi = T;  // smallest pos > prev with F(pos) >= target
-    while (lo < hi) {
-      const long long mid = (lo + hi) / 2;
-      if (F(mid) >= target) hi = mid;
-      else lo = mid + 1;
-    }
+    long long pos = F_inverse(target);                      // smallest pos > prev with F(pos) >= target
+    pos = pos > prev ? pos : prev + 1;
     bal[used++] = prev;
-    prev = lo;
+    prev = pos < T ? pos : T;
   }
   bal[used] = T;
   const bool use_bal = sk_max_cost(bal, used, n_kv) <= sk_max_cost(even, parts, n_kv);

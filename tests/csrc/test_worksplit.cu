@@ -3,14 +3,45 @@
 // host code): for many (units, KV tiles, clusters) it checks that every
 // (unit, KV tile) iteration is processed exactly once, that pieces of split
 // units get distinct partial-result slots, and that the combine kernel's slot
-// lookup finds exactly the pieces the kernel wrote. Prints "ok" and exits 0 on
-// success.
+// lookup finds exactly the pieces the kernel wrote. The planner's cut points
+// are checked against a brute-force restatement (linear search over the
+// cumulative cost). Prints "ok" and exits 0 on success.
 #include <cstdio>
 #include <map>
 #include <set>
 #include <vector>
 
 #include "../../llm_fa_b200/csrc/fa_fwd_kernel.cuh"
+
+// Brute-force cut: range c starts at the smallest pos > start of range c - 1
+// with F(pos) >= ceil(F(T) c / parts), F(pos) = pos + kSegmentCost *
+// floor((pos - 1) / n_kv); the even cut is floor(T c / parts). The planner
+// keeps the cut whose largest range cost is smaller (ties: balanced).
+static std::vector<long long> brute_bounds(long long T, int parts, int n_kv) {
+  auto F = [&](long long pos) -> long long {
+    return pos <= 0 ? 0 : pos + llmfa::kSegmentCost * ((pos - 1) / n_kv);
+  };
+  auto max_cost = [&](const std::vector<long long>& b) {
+    long long worst = 0;
+    for (size_t c = 0; c + 1 < b.size(); ++c) {
+      long long cost = 0;
+      for (long long it = b[c]; it < b[c + 1]; ++it)
+        cost += 1 + (it > b[c] && it % n_kv == 0 ? llmfa::kSegmentCost : 0);
+      worst = cost > worst ? cost : worst;
+    }
+    return worst;
+  };
+  std::vector<long long> even(parts + 1), bal(1, 0);
+  for (int c = 0; c <= parts; ++c) even[c] = T * c / parts;
+  for (int c = 1; c <= parts && bal.back() < T; ++c) {
+    const long long target = (F(T) * c + parts - 1) / parts;
+    long long pos = bal.back() + 1;
+    while (pos < T && F(pos) < target) ++pos;
+    bal.push_back(pos);
+  }
+  bal.back() = T;
+  return max_cost(bal) <= max_cost(even) ? bal : even;
+}
 
 static int check(int n_units, int n_kv, int G, bool sk) {
   llmfa::FwdParams p{};
@@ -30,6 +61,10 @@ static int check(int n_units, int n_kv, int G, bool sk) {
     if (p.sk_clusters < 2 || p.sk_clusters > parts) return 9;
     for (int c = 0; c < p.sk_clusters; ++c)  // non-empty ranges
       if (p.sk_bound[c + 1] <= p.sk_bound[c] && c + 1 < p.sk_clusters) return 10;
+    const std::vector<long long> b = brute_bounds(total, static_cast<int>(parts), n_kv);
+    if (static_cast<int>(b.size()) != p.sk_clusters + 1) return 11;
+    for (int c = 0; c <= p.sk_clusters; ++c)
+      if (p.sk_bound[c] != b[c]) return 11;
     grid = dp > 0 ? G : p.sk_clusters;
   }
   std::vector<int> seen(static_cast<size_t>(n_units) * n_kv, 0);
