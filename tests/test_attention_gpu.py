@@ -287,6 +287,40 @@ def test_split_kv_matches_unsplit_and_oracle(B, H, Sq, Sk):
     _assert_close(o_split, o_whole.float(), 8e-3, 5e-4)
 
 
+@pytest.mark.parametrize("B,H,Sq,Sk", [(1, 1, 16384, 4096), (1, 1, 512, 131072)])
+def test_workspace_contents_do_not_matter(B, H, Sq, Sk):
+    """Split-KV results are the same whether the workspace holds garbage, zeros or the
+    previous call's partial results (nothing is read that the same call did not write);
+    (1, 1, 512, 131072) cuts its one query block across every cluster."""
+    from llm_fa_b200.attention import workspace_size
+    plan = launch_plan(B, H, Sq, Sk)
+    assert plan["kernels"] == 2 and plan["split_units"] > 0, plan
+    cfg = Config("m", B, H, Sq, Sk, seed=Sq + Sk + 5 * H)
+    q, k, v = make_inputs(cfg)
+    qd, kd, vd = q.cuda(), k.cuda(), v.cuda()
+    ws_bytes = workspace_size()
+    ws = torch.empty(ws_bytes, dtype=torch.uint8, device="cuda")
+    outs = []
+    for fill in (0xFF, 0x00, None):  # garbage, zeros, the previous call's contents
+        if fill is not None:
+            ws.fill_(fill)
+        o = torch.full_like(qd, float("nan"))
+        rc = _lib.lib().llmfa_forward(
+            ctypes.c_void_p(qd.data_ptr()), _lib.strides3(qd.stride()[:3]),
+            ctypes.c_void_p(kd.data_ptr()), _lib.strides3(kd.stride()[:3]),
+            ctypes.c_void_p(vd.data_ptr()), _lib.strides3(vd.stride()[:3]),
+            ctypes.c_void_p(o.data_ptr()), _lib.strides3(o.stride()[:3]),
+            B, H, Sq, Sk, ctypes.c_float(cfg.scale), ctypes.c_void_p(ws.data_ptr()), ws_bytes,
+            ctypes.c_void_p(torch.cuda.current_stream().cuda_stream))
+        _lib.check(rc, "llmfa_forward")
+        torch.cuda.synchronize()
+        assert device_status() == 0
+        outs.append(o.cpu())
+    assert torch.equal(outs[0], outs[1]) and torch.equal(outs[0], outs[2])
+    rows = sample_rows(cfg, 512)
+    _assert_close(outs[0][:, rows], sdpa_fp32(q, k, v, rows=rows))
+
+
 # ----------------------------------------------------------------- reference surface
 def test_mirror_module_surface():
     torch.manual_seed(0)
