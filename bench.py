@@ -61,6 +61,9 @@ def parse_args():
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--validate", action="store_true", help="NCCL-gather O to rank 0 afterwards")
     ap.add_argument("--cpu-seconds", type=float, default=10.0, help="CPU baseline sample budget")
+    ap.add_argument("--sweep", action="store_true",
+                    help="time this kernel and the reference kernel on the reference's eight "
+                         "published single-head shapes (one JSON line per shape)")
     return ap.parse_args()
 
 
@@ -421,8 +424,62 @@ def run_reference(args, cfg, world, rank, local):
     return line
 
 
+# The reference's published single-head shapes (q, sk), README.md:58-65 of the reference.
+SWEEP_SHAPES = [(q, sk) for q in (16384, 32768) for sk in (16384, 32768, 65536, 131072)]
+
+
+def run_sweep(args) -> None:
+    """This kernel and the reference's llm_fa.cu kernel (oracle/_ref) on the same GPU, on
+    the reference's published shapes: CUDA events around each call, a 256 MiB L2 flush
+    before every call, median of --steps calls after --warmup; also the largest
+    difference between the two outputs."""
+    import statistics
+
+    import torch
+
+    from llm_fa_b200 import attention_forward, device_status
+    from oracle.build_ref import load_module
+    mod = load_module()
+    dev = torch.device("cuda", 0)
+    flush = torch.empty(L2_FLUSH_BYTES, dtype=torch.uint8, device=dev)
+    gen = torch.Generator(device="cpu").manual_seed(0)
+
+    def median_us(fn):
+        ts = []
+        for i in range(args.warmup + args.steps):
+            flush.zero_()
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record()
+            fn()
+            e1.record()
+            torch.cuda.synchronize()
+            if i >= args.warmup:
+                ts.append(e0.elapsed_time(e1) * 1e3)
+        return statistics.median(ts)
+
+    for q_len, sk in SWEEP_SHAPES:
+        Q, K, V = (torch.randn(n, 128, generator=gen).bfloat16().to(dev)
+                   for n in (q_len, sk, sk))
+        O = torch.empty_like(Q)
+        t_ours = median_us(lambda: attention_forward(Q, K, V, out=O))
+        t_ref = median_us(lambda: mod.llm_fa_forward(Q, K, V))
+        diff = (O.float() - mod.llm_fa_forward(Q, K, V)[0].float()).abs().max().item()
+        flops = 4 * q_len * sk * 128
+        print(json.dumps({"q": q_len, "sk": sk, "ours_us": round(t_ours, 1),
+                          "reference_us": round(t_ref, 1),
+                          "speedup": round(t_ref / t_ours, 3),
+                          "ours_tflops": round(flops / t_ours / 1e6, 1),
+                          "reference_tflops": round(flops / t_ref / 1e6, 1),
+                          "max_abs_diff_vs_reference": diff}), flush=True)
+    if device_status() != 0:
+        raise RuntimeError(f"device status {device_status()}")
+
+
 def main():
     args = parse_args()
+    if args.sweep:
+        run_sweep(args)
+        return
     world, rank, local = dist_env()
     if world != args.gpus:
         print(f"# note: --gpus {args.gpus} but WORLD_SIZE={world}; using WORLD_SIZE",
