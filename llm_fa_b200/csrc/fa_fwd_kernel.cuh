@@ -137,6 +137,7 @@ enum WaitSite : int {
   kSiteEpiOFull = 9,
   kSiteEpiStage = 10,
   kSiteDrain = 11,
+  kSiteCombine = 12,
 };
 
 // ---------------------------------------------------------------- event trace
@@ -1129,14 +1130,19 @@ __host__ __device__ __forceinline__ int piece_slot(int c_lo, int slot_lo, int c)
 // Finishes the units that stream-K mode cut across clusters: for every query
 // row, O = sum_p w_p O_p / sum_p w_p with w_p = l_p 2^(m_p - m) over the
 // pieces p (O_p normalised by l_p, m = max_p m_p), the standard merge of
-// partial softmax states. The host
-// lists the split units and their pieces. A warp merges 4 rows, one float4
-// column group per lane (coalesced 512-byte rows); the loads of up to four
-// pieces are issued together, and more pieces are folded in groups of four
-// with a running maximum, so a warp waits on memory about once per group.
+// partial softmax states. The host lists the split units and their pieces.
+// A CTA merges 32 rows of one unit: one thread issues bulk copies of those
+// rows of every piece (8 KB of O plus m and l each, up to 8 pieces per round)
+// into shared memory, so a CTA has all its bytes in flight at once; each of
+// the 256 threads then merges 16 columns of one row. Pieces are folded in
+// groups of four with a running maximum.
 constexpr int kCombineMaxUnits = 160;  // > clusters of any B200 grid (split units < clusters)
-constexpr int kCombineRowsPerWarp = 4;
-constexpr int kCombineWarpsPerCta = 8;
+constexpr int kCombineRows = 32;       // query rows per CTA
+constexpr int kCombineThreads = 256;   // 8 threads per row
+constexpr int kCombineBlocksPerUnit = kUnitRows / kCombineRows;
+constexpr uint32_t kCombineOBytes = kCombineRows * kHeadDim * 2;            // 8 KB
+constexpr uint32_t kCombinePieceBytes = kCombineOBytes + 2 * kCombineRows * 4;  // + m, l
+constexpr int kCombineMaxRound = 8;    // pieces per load round
 struct CombineParams {
   const uint16_t* ws_o;         // [slots * 512, 128] bf16 normalised partial O
   const float* ws_ml;           // [slots][m 512, l 512]
@@ -1144,85 +1150,113 @@ struct CombineParams {
   long long o_sb, o_ss, o_sh;
   float* lse;                   // optional log-sum-exp output (see FwdParams)
   long long lse_sb, lse_sh;
+  WaitCtl wait;
   int H, Sq, n_qblk, n_split;
+  int round_pieces;             // pieces per load round: min(most pieces of a unit, 8)
   int unit[kCombineMaxUnits];   // split units
   short c_lo[kCombineMaxUnits], np[kCombineMaxUnits], slot_lo[kCombineMaxUnits];
 };
 
-__global__ void __launch_bounds__(kCombineWarpsPerCta * 32)
+__global__ void __launch_bounds__(kCombineThreads)
     llm_fa_combine_kernel(const __grid_constant__ CombineParams p) {
+  extern __shared__ __align__(128) uint8_t cmb_smem[];
+  __shared__ __align__(8) uint64_t cmb_bar;
+  const uint32_t sbase = ptx::smem_u32(cmb_smem);
+  const uint32_t bar = ptx::smem_u32(&cmb_bar);
+  const int tid = static_cast<int>(threadIdx.x);
+  if (tid == 0) {
+    ptx::mbar_init(bar, 1);
+    ptx::fence_mbar_init();
+  }
+  __syncthreads();
   // Launched as a programmatic dependent of the attention kernel: everything
   // before this wait overlaps that kernel's tail; nothing is read before it.
   asm volatile("griddepcontrol.wait;" ::: "memory");
-  constexpr int kWarpsPerUnit = kUnitRows / kCombineRowsPerWarp;
-  const int lane = threadIdx.x & 31;
-  const int gw = blockIdx.x * kCombineWarpsPerCta + static_cast<int>(threadIdx.x >> 5);
-  const int i = gw / kWarpsPerUnit;
+  const int i = static_cast<int>(blockIdx.x) / kCombineBlocksPerUnit;
   if (i >= p.n_split) return;
+  const int row0 = (static_cast<int>(blockIdx.x) - i * kCombineBlocksPerUnit) * kCombineRows;
   const int u = p.unit[i];
   const int c_lo = p.c_lo[i], np = p.np[i], slot_lo = p.slot_lo[i];
-  const int row0 = (gw - i * kWarpsPerUnit) * kCombineRowsPerWarp;
-  float m[kCombineRowsPerWarp], wsum[kCombineRowsPerWarp];
-  float4 acc[kCombineRowsPerWarp];
+  const int r = tid >> 3;        // row of this CTA's 32
+  const int ca = tid & 7;        // 16-byte column chunks ca and ca + 8 (columns 8 ca.., 64 + 8 ca..)
+  float m = -INFINITY, wsum = 0.f, acc[16];
 #pragma unroll
-  for (int r = 0; r < kCombineRowsPerWarp; ++r) {
-    m[r] = -INFINITY;
-    wsum[r] = 0.f;
-    acc[r] = make_float4(0.f, 0.f, 0.f, 0.f);
-  }
-  for (int g = 0; g < np; g += 4) {
-    float pm[4][kCombineRowsPerWarp], pl[4][kCombineRowsPerWarp];
-    uint2 pv[4][kCombineRowsPerWarp];
-#pragma unroll
-    for (int k = 0; k < 4; ++k) {
-      const bool have = g + k < np;
-      const long long slot = piece_slot(c_lo, slot_lo, c_lo + g + k);
-      const float* ml = p.ws_ml + slot * kSlotMLFloats;
-      const uint16_t* so = p.ws_o + slot * (kSlotRows * kHeadDim);
-#pragma unroll
-      for (int r = 0; r < kCombineRowsPerWarp; ++r) {
-        pm[k][r] = have ? __ldg(ml + row0 + r) : -INFINITY;
-        pl[k][r] = have ? __ldg(ml + kSlotRows + row0 + r) : 0.f;
-        pv[k][r] = have ? __ldg(reinterpret_cast<const uint2*>(so + (row0 + r) * kHeadDim) + lane)
-                        : make_uint2(0u, 0u);
+  for (int e = 0; e < 16; ++e) acc[e] = 0.f;
+  uint32_t phase = 0;
+  bool ok = true;
+  for (int g0 = 0; g0 < np && ok; g0 += p.round_pieces) {
+    const int n_here = np - g0 < p.round_pieces ? np - g0 : p.round_pieces;
+    if (tid == 0) {
+      ptx::mbar_arrive_expect_tx(bar, static_cast<uint32_t>(n_here) * kCombinePieceBytes);
+      for (int k = 0; k < n_here; ++k) {
+        const long long slot = piece_slot(c_lo, slot_lo, c_lo + g0 + k);
+        const uint32_t dst = sbase + static_cast<uint32_t>(k) * kCombinePieceBytes;
+        const float* ml = p.ws_ml + slot * kSlotMLFloats + row0;
+        ptx::bulk_load(dst, p.ws_o + (slot * kSlotRows + row0) * kHeadDim, kCombineOBytes, bar);
+        ptx::bulk_load(dst + kCombineOBytes, ml, kCombineRows * 4, bar);
+        ptx::bulk_load(dst + kCombineOBytes + kCombineRows * 4, ml + kSlotRows, kCombineRows * 4,
+                       bar);
       }
     }
+    ok = mbar_wait(bar, phase, p.wait, kSiteCombine, false);
+    phase ^= 1u;
+    if (ok) {
+      for (int g = 0; g < n_here; g += 4) {
+        float pm[4], pl[4];
 #pragma unroll
-    for (int r = 0; r < kCombineRowsPerWarp; ++r) {
-      const float mn = fmaxf(fmaxf(m[r], fmaxf(pm[0][r], pm[1][r])), fmaxf(pm[2][r], pm[3][r]));
-      const float sc = ptx::ex2_mufu(m[r] - mn);  // 0 on the first group (m = -inf)
-      wsum[r] *= sc;
-      acc[r].x *= sc;
-      acc[r].y *= sc;
-      acc[r].z *= sc;
-      acc[r].w *= sc;
+        for (int k = 0; k < 4; ++k) {
+          const uint32_t pb = sbase + static_cast<uint32_t>(g + k) * kCombinePieceBytes + kCombineOBytes;
+          const bool have = g + k < n_here;
+          pm[k] = have ? ptx::ld_shared_f32(pb + r * 4) : -INFINITY;
+          pl[k] = have ? ptx::ld_shared_f32(pb + (kCombineRows + r) * 4) : 0.f;
+        }
+        const float mn = fmaxf(fmaxf(m, fmaxf(pm[0], pm[1])), fmaxf(pm[2], pm[3]));
+        const float sc = ptx::ex2_mufu(m - mn);  // 0 on the first group (m = -inf)
+        wsum *= sc;
 #pragma unroll
-      for (int k = 0; k < 4; ++k) {
-        const float w = pl[k][r] * ptx::ex2_mufu(pm[k][r] - mn);  // 0 for absent pieces
-        wsum[r] += w;
-        acc[r].x += w * __uint_as_float(pv[k][r].x << 16);
-        acc[r].y += w * __uint_as_float(pv[k][r].x & 0xFFFF0000u);
-        acc[r].z += w * __uint_as_float(pv[k][r].y << 16);
-        acc[r].w += w * __uint_as_float(pv[k][r].y & 0xFFFF0000u);
+        for (int e = 0; e < 16; ++e) acc[e] *= sc;
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+          if (g + k >= n_here) break;
+          const float w = pl[k] * ptx::ex2_mufu(pm[k] - mn);
+          wsum += w;
+          const uint32_t ob = sbase + static_cast<uint32_t>(g + k) * kCombinePieceBytes +
+                              r * (kHeadDim * 2);
+#pragma unroll
+          for (int h = 0; h < 2; ++h) {
+            const uint4 v = ptx::ld_shared_v4(ob + (ca + 8 * h) * 16);
+            const uint32_t x[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+            for (int e = 0; e < 4; ++e) {
+              acc[8 * h + 2 * e] += w * __uint_as_float(x[e] << 16);
+              acc[8 * h + 2 * e + 1] += w * __uint_as_float(x[e] & 0xFFFF0000u);
+            }
+          }
+        }
+        m = mn;
       }
-      m[r] = mn;
     }
+    ok = __syncthreads_and(ok) != 0;  // the round's shared memory has been read
   }
+  if (!ok) return;
   const int bh = u / p.n_qblk;
   const int qb = u - bh * p.n_qblk;
   const int b = bh / p.H, h = bh - (bh / p.H) * p.H;
+  const int srow = qb * kUnitRows + row0 + r;
+  if (srow >= p.Sq) return;
+  const float inv = 1.f / wsum;
+  uint16_t* orow = p.o + b * p.o_sb + srow * p.o_ss + h * p.o_sh;
 #pragma unroll
-  for (int r = 0; r < kCombineRowsPerWarp; ++r) {
-    const int srow = qb * kUnitRows + row0 + r;
-    if (srow >= p.Sq) break;
-    const float inv = 1.f / wsum[r];
-    uint2 pk;
-    pk.x = ptx::bf16x2_pack(acc[r].x * inv, acc[r].y * inv);
-    pk.y = ptx::bf16x2_pack(acc[r].z * inv, acc[r].w * inv);
-    *reinterpret_cast<uint2*>(p.o + b * p.o_sb + srow * p.o_ss + h * p.o_sh + lane * 4) = pk;
-    if (p.lse != nullptr && lane == 0)  // sum = 2^m * sum_p w_p
-      p.lse[b * p.lse_sb + h * p.lse_sh + srow] = (m[r] + __log2f(wsum[r])) * 0.6931471805599453f;
+  for (int hh = 0; hh < 2; ++hh) {
+    uint4 pk;
+    pk.x = ptx::bf16x2_pack(acc[8 * hh + 0] * inv, acc[8 * hh + 1] * inv);
+    pk.y = ptx::bf16x2_pack(acc[8 * hh + 2] * inv, acc[8 * hh + 3] * inv);
+    pk.z = ptx::bf16x2_pack(acc[8 * hh + 4] * inv, acc[8 * hh + 5] * inv);
+    pk.w = ptx::bf16x2_pack(acc[8 * hh + 6] * inv, acc[8 * hh + 7] * inv);
+    *reinterpret_cast<uint4*>(orow + (ca + 8 * hh) * 8) = pk;
   }
+  if (p.lse != nullptr && ca == 0)  // sum = 2^m * sum_p w_p
+    p.lse[b * p.lse_sb + h * p.lse_sh + srow] = (m + __log2f(wsum)) * 0.6931471805599453f;
 }
 
 }  // namespace llmfa

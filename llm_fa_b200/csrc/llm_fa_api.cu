@@ -83,7 +83,11 @@ int device_setup(int* dev_out, DeviceSetup** out) {
                              static_cast<int>(llmfa::kSmemBytes)) != cudaSuccess ||
         cudaFuncSetAttribute(llmfa::llm_fa_kernel_sm100<true>,
                              cudaFuncAttributeMaxDynamicSharedMemorySize,
-                             static_cast<int>(llmfa::kSmemBytes)) != cudaSuccess) {
+                             static_cast<int>(llmfa::kSmemBytes)) != cudaSuccess ||
+        cudaFuncSetAttribute(llmfa::llm_fa_combine_kernel,
+                             cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             static_cast<int>(llmfa::kCombineMaxRound *
+                                              llmfa::kCombinePieceBytes)) != cudaSuccess) {
       cudaGetLastError();
       s.err = LLMFA_ERR_CUDA;
       return;
@@ -183,18 +187,21 @@ int make_plan(llmfa::FwdParams& p, int G, bool have_workspace) {
 // The units of a stream-K launch that were cut across clusters, with their
 // pieces, in the combine kernel's table; returns how many.
 int list_split_units(const llmfa::FwdParams& p, llmfa::CombineParams* cp) {
-  int n = 0;
+  int n = 0, most = 0;
   for (int u = p.dp_units; u < p.n_units; ++u) {
     const llmfa::UnitPieces pc = llmfa::unit_pieces(p, u);
     if (pc.c_lo == pc.c_hi) continue;  // one cluster computed the whole unit
+    const int np = pc.c_hi - pc.c_lo + 1;
+    most = np > most ? np : most;
     if (cp != nullptr) {
       cp->unit[n] = u;
       cp->c_lo[n] = static_cast<short>(pc.c_lo);
-      cp->np[n] = static_cast<short>(pc.c_hi - pc.c_lo + 1);
+      cp->np[n] = static_cast<short>(np);
       cp->slot_lo[n] = static_cast<short>(pc.slot_lo);
     }
     ++n;
   }
+  if (cp != nullptr) cp->round_pieces = most < llmfa::kCombineMaxRound ? most : llmfa::kCombineMaxRound;
   return n;
 }
 
@@ -353,16 +360,16 @@ int llmfa_forward_lse(const void* q, const int64_t q_strides[3], const void* k,
     cp.lse = p.lse;
     cp.lse_sb = p.lse_sb;
     cp.lse_sh = p.lse_sh;
+    cp.wait = p.wait;
     cp.H = p.H;
     cp.Sq = p.Sq;
     cp.n_qblk = p.n_qblk;
     cp.n_split = list_split_units(p, &cp);
     if (cp.n_split > 0) {
-      constexpr int kWarpsPerUnit = llmfa::kUnitRows / llmfa::kCombineRowsPerWarp;
       cudaLaunchConfig_t cfg{};
-      cfg.gridDim = dim3((cp.n_split * kWarpsPerUnit + llmfa::kCombineWarpsPerCta - 1) /
-                         llmfa::kCombineWarpsPerCta);
-      cfg.blockDim = dim3(llmfa::kCombineWarpsPerCta * 32);
+      cfg.gridDim = dim3(cp.n_split * llmfa::kCombineBlocksPerUnit);
+      cfg.blockDim = dim3(llmfa::kCombineThreads);
+      cfg.dynamicSmemBytes = static_cast<size_t>(cp.round_pieces) * llmfa::kCombinePieceBytes;
       cfg.stream = st;
       // Programmatic dependent launch: the combine grid is scheduled while the
       // attention kernel's last CTAs finish and waits (griddepcontrol.wait)
