@@ -217,7 +217,7 @@ __device__ __forceinline__ uint32_t cta_aborted() {
 __device__ __forceinline__ void cta_abort() { *static_cast<volatile uint32_t*>(&g_cta_abort) = 1u; }
 
 constexpr int kMaxSkParts = 160;  // stream-K ranges (<= clusters of the grid)
-constexpr int kSegmentCost = 1;   // a segment switch costs about this many KV tiles
+constexpr int kSegmentCost = 2;   // a segment switch costs about this many KV tiles
 
 struct FwdParams {
   int B, H, Sq, Sk;

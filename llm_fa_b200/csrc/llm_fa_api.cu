@@ -161,7 +161,7 @@ int encode_bshd(CUtensorMap* m, const void* ptr, const int64_t* st, int64_t seq,
 // KV-tile steps the cut saves the busiest cluster outweigh what the split
 // costs. Cost model, fitted to 22 shapes timed both ways on B200 (it picks
 // the faster schedule for all of them): a KV-tile step ~2 us; the split
-// ~2 us plus ~0.15 us per cut unit (combine kernel, the pieces' epilogues).
+// ~1 us plus ~0.15 us per cut unit (combine kernel, the pieces' epilogues).
 // Fills the work-split fields of `p` (n_units, n_kv set) and returns the grid
 // size in 2-CTA clusters.
 int make_plan(llmfa::FwdParams& p, int G, bool have_workspace) {
@@ -178,12 +178,12 @@ int make_plan(llmfa::FwdParams& p, int G, bool have_workspace) {
   if (parts > llmfa::kMaxSkParts) parts = llmfa::kMaxSkParts;
   if (parts < 2 || n_units - dp_units > llmfa::kCombineMaxUnits) return classic;
   // KV-tile steps of the busiest cluster: classic = waves x n_kv; stream-K =
-  // the full waves, an even share of the cut iterations and one segment switch.
+  // the full waves, an even share of the cut iterations and a segment switch.
   const long long classic_steps = static_cast<long long>(waves) * p.n_kv;
   const long long sk_steps = static_cast<long long>(dp_units / G) * p.n_kv +
                              (sk_total + parts - 1) / parts + llmfa::kSegmentCost;
   const double saved_us = 2.0 * static_cast<double>(classic_steps - sk_steps);
-  const double split_us = 2.0 + 0.15 * static_cast<double>(n_units - dp_units);
+  const double split_us = 1.0 + 0.15 * static_cast<double>(n_units - dp_units);
   if (saved_us <= split_us) return classic;
   p.sk_mode = 1;
   p.dp_units = dp_units;
