@@ -94,6 +94,16 @@ class HostAttention:
                 out.copy_(slot["o"], non_blocking=True)
                 copied_out = torch.cuda.Event()
                 copied_out.record(self.s_out)
+            # The slot's buffers come from the caching allocator on the current
+            # stream; when a later request of another shape replaces them, they
+            # must not be handed out again before this work on the three
+            # streams has finished.
+            for name, streams in (("q", (self.s_in, self.s_compute)),
+                                  ("k", (self.s_in, self.s_compute)),
+                                  ("v", (self.s_in, self.s_compute)),
+                                  ("o", (self.s_compute, self.s_out))):
+                for st in streams:
+                    slot[name].record_stream(st)
         slot["computed"], slot["copied_out"] = computed, copied_out
         return copied_out
 
