@@ -321,6 +321,9 @@ def run_ours(args, cfg, world, rank, local):
     line = {
         "metric": METRIC, "value": round(value, 2), "unit": UNIT, "n_gpus": world,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(mean_ms_max, 5),
+        # this rank's spread of the step times behind the mean
+        "ms_per_step_median": round(statistics.median(times_ms), 5),
+        "ms_per_step_min": round(min(times_ms), 5),
         "higher_is_better": True,
         "scaling": "strong" if shard[0] in ("heads", "batch") else "weak",
         "vs_baseline": (round(value / world / PUBLISHED_REF_TFLOPS[cfg.name], 3)
