@@ -217,6 +217,7 @@ __device__ __forceinline__ uint32_t cta_aborted() {
 __device__ __forceinline__ void cta_abort() { *static_cast<volatile uint32_t*>(&g_cta_abort) = 1u; }
 
 constexpr int kMaxSkParts = 160;  // stream-K ranges (<= clusters of the grid)
+constexpr int kCombineMaxUnits = 160;  // > clusters of any B200 grid (split units < clusters)
 constexpr int kSegmentCost = 2;   // a segment switch costs about this many KV tiles
 
 struct FwdParams {
@@ -368,6 +369,47 @@ inline void plan_sk_bounds(FwdParams& p, int parts, int n_kv) {
   p.sk_clusters = use_bal ? used : parts;
   for (int c = 0; c <= kMaxSkParts; ++c)
     p.sk_bound[c] = c <= p.sk_clusters ? (use_bal ? bal[c] : even[c]) : T;
+}
+
+// Launch plan of one forward: classic persistent schedule, or stream-K over
+// the last partial wave of units when a large enough workspace is given, the
+// classic schedule would leave more than 2% of the clusters idle, and the
+// KV-tile steps the cut saves the busiest cluster outweigh what the split
+// costs. Cost model, fitted to 22 shapes timed both ways on B200 (it picks
+// the faster schedule for all of them): a KV-tile step ~2 us; the split
+// ~1 us plus ~0.15 us per cut unit (combine kernel, the pieces' epilogues).
+// Fills the work-split fields of `p` (n_units, n_kv set) and returns the grid
+// size in 2-CTA clusters.
+inline int make_plan(FwdParams& p, int G, bool have_workspace) {
+  p.sk_mode = 0;
+  const int n_units = p.n_units;
+  const int waves = (n_units + G - 1) / G;
+  const double classic_eff = static_cast<double>(n_units) / (static_cast<double>(G) * waves);
+  const int classic = n_units < G ? n_units : G;
+  if (!have_workspace || classic_eff >= 0.98) return classic;
+  const int dp_units = (n_units / G) * G;
+  const long long sk_total = static_cast<long long>(n_units - dp_units) * p.n_kv;
+  long long parts = sk_total / 4;  // at least 4 KV tiles per piece
+  if (parts > G) parts = G;
+  if (parts > kMaxSkParts) parts = kMaxSkParts;
+  if (parts < 2 || n_units - dp_units > kCombineMaxUnits) return classic;
+  // KV-tile steps of the busiest cluster: classic = waves x n_kv; stream-K =
+  // the full waves, an even share of the cut iterations and a segment switch.
+  const long long classic_steps = static_cast<long long>(waves) * p.n_kv;
+  const long long sk_steps = static_cast<long long>(dp_units / G) * p.n_kv +
+                             (sk_total + parts - 1) / parts + kSegmentCost;
+  const double saved_us = 2.0 * static_cast<double>(classic_steps - sk_steps);
+  const double split_us = 1.0 + 0.15 * static_cast<double>(n_units - dp_units);
+  if (saved_us <= split_us) return classic;
+  p.sk_mode = 1;
+  p.dp_units = dp_units;
+  p.sk_total = sk_total;
+  plan_sk_bounds(p, static_cast<int>(parts), p.n_kv);
+  if (p.sk_clusters < 2) {
+    p.sk_mode = 0;
+    return classic;
+  }
+  return dp_units > 0 ? G : p.sk_clusters;
 }
 
 struct SegIter {
@@ -1136,7 +1178,6 @@ __host__ __device__ __forceinline__ int piece_slot(int c_lo, int slot_lo, int c)
 // into shared memory, so a CTA has all its bytes in flight at once; each of
 // the 256 threads then merges 16 columns of one row. Pieces are folded in
 // groups of four with a running maximum.
-constexpr int kCombineMaxUnits = 160;  // > clusters of any B200 grid (split units < clusters)
 constexpr int kCombineRows = 32;       // query rows per CTA
 constexpr int kCombineThreads = 256;   // 8 threads per row
 constexpr int kCombineBlocksPerUnit = kUnitRows / kCombineRows;

@@ -155,47 +155,6 @@ int encode_bshd(CUtensorMap* m, const void* ptr, const int64_t* st, int64_t seq,
   return r == CUDA_SUCCESS ? LLMFA_OK : LLMFA_ERR_TENSOR_MAP;
 }
 
-// Launch plan of one forward: classic persistent schedule, or stream-K over
-// the last partial wave of units when a large enough workspace is given, the
-// classic schedule would leave more than 2% of the clusters idle, and the
-// KV-tile steps the cut saves the busiest cluster outweigh what the split
-// costs. Cost model, fitted to 22 shapes timed both ways on B200 (it picks
-// the faster schedule for all of them): a KV-tile step ~2 us; the split
-// ~1 us plus ~0.15 us per cut unit (combine kernel, the pieces' epilogues).
-// Fills the work-split fields of `p` (n_units, n_kv set) and returns the grid
-// size in 2-CTA clusters.
-int make_plan(llmfa::FwdParams& p, int G, bool have_workspace) {
-  p.sk_mode = 0;
-  const int n_units = p.n_units;
-  const int waves = (n_units + G - 1) / G;
-  const double classic_eff = static_cast<double>(n_units) / (static_cast<double>(G) * waves);
-  const int classic = n_units < G ? n_units : G;
-  if (!have_workspace || classic_eff >= 0.98) return classic;
-  const int dp_units = (n_units / G) * G;
-  const long long sk_total = static_cast<long long>(n_units - dp_units) * p.n_kv;
-  long long parts = sk_total / 4;  // at least 4 KV tiles per piece
-  if (parts > G) parts = G;
-  if (parts > llmfa::kMaxSkParts) parts = llmfa::kMaxSkParts;
-  if (parts < 2 || n_units - dp_units > llmfa::kCombineMaxUnits) return classic;
-  // KV-tile steps of the busiest cluster: classic = waves x n_kv; stream-K =
-  // the full waves, an even share of the cut iterations and a segment switch.
-  const long long classic_steps = static_cast<long long>(waves) * p.n_kv;
-  const long long sk_steps = static_cast<long long>(dp_units / G) * p.n_kv +
-                             (sk_total + parts - 1) / parts + llmfa::kSegmentCost;
-  const double saved_us = 2.0 * static_cast<double>(classic_steps - sk_steps);
-  const double split_us = 1.0 + 0.15 * static_cast<double>(n_units - dp_units);
-  if (saved_us <= split_us) return classic;
-  p.sk_mode = 1;
-  p.dp_units = dp_units;
-  p.sk_total = sk_total;
-  llmfa::plan_sk_bounds(p, static_cast<int>(parts), p.n_kv);
-  if (p.sk_clusters < 2) {
-    p.sk_mode = 0;
-    return classic;
-  }
-  return dp_units > 0 ? G : p.sk_clusters;
-}
-
 // The units of a stream-K launch that were cut across clusters, with their
 // pieces, in the combine kernel's table; returns how many.
 int list_split_units(const llmfa::FwdParams& p, llmfa::CombineParams* cp) {
@@ -341,7 +300,7 @@ int llmfa_forward_lse(const void* q, const int64_t q_strides[3], const void* k,
   const int G = s->max_clusters;
   const uint64_t need = static_cast<uint64_t>(2 * G) * llmfa::kSlotBytes;
   const int nclusters =
-      make_plan(p, G, workspace != nullptr && workspace_bytes >= need && aligned16(workspace));
+      llmfa::make_plan(p, G, workspace != nullptr && workspace_bytes >= need && aligned16(workspace));
   if (p.sk_mode) {
     p.ws_ml = reinterpret_cast<float*>(static_cast<char*>(workspace) +
                                        static_cast<uint64_t>(2 * G) * llmfa::kSlotOBytes);
@@ -454,7 +413,7 @@ int llmfa_launch_plan(int64_t batch, int64_t heads, int64_t seq_q, int64_t seq_k
   p.n_units = n_units;
   p.n_kv = n_kv;
   const int nclusters =
-      make_plan(p, G, workspace_bytes >= static_cast<uint64_t>(2 * G) * llmfa::kSlotBytes);
+      llmfa::make_plan(p, G, workspace_bytes >= static_cast<uint64_t>(2 * G) * llmfa::kSlotBytes);
   const int n_split = p.sk_mode ? list_split_units(p, nullptr) : 0;
   *kernels = n_split > 0 ? 2 : 1;
   *clusters = nclusters;

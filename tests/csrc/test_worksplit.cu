@@ -5,7 +5,9 @@
 // units get distinct partial-result slots, and that the combine kernel's slot
 // lookup finds exactly the pieces the kernel wrote. The planner's cut points
 // are checked against a brute-force restatement (linear search over the
-// cumulative cost). Prints "ok" and exits 0 on success.
+// cumulative cost). The launch planner's choice between the classic schedule
+// and stream-K is checked against shapes timed both ways on a B200 (74
+// clusters). Prints "ok" and exits 0 on success.
 #include <cstdio>
 #include <map>
 #include <set>
@@ -106,7 +108,45 @@ static int check(int n_units, int n_kv, int G, bool sk) {
   return 0;
 }
 
+// (B, H, Sq, Sk) and whether stream-K measured faster than the classic
+// schedule on one B200 (CUDA events, L2 flushed, median of 10 calls each).
+struct Timed {
+  int B, H, Sq, Sk;
+  bool sk_faster;
+};
+static const Timed kTimed[] = {
+    {1, 2, 1024, 1024, true},    {1, 1, 2048, 2048, true},   {1, 1, 4096, 4096, true},
+    {1, 2, 2048, 8192, true},    {1, 4, 4096, 2048, true},   {1, 8, 2048, 2048, true},
+    {1, 16, 1024, 4096, true},   {2, 16, 2048, 2048, false}, {1, 1, 8192, 8192, true},
+    {1, 1, 16384, 16384, true},  {2, 16, 2048, 4096, true},  {2, 16, 2048, 8192, true},
+    {2, 16, 2048, 16384, true},  {1, 40, 2048, 2048, true},  {3, 16, 2048, 2048, true},
+    {4, 16, 2048, 2048, true},   {1, 80, 1024, 1024, true},  {1, 100, 1024, 4096, true},
+    {1, 50, 2048, 1024, false},  {1, 3, 1024, 1024, true},   {1, 6, 1024, 2048, true},
+    {1, 1, 1024, 4096, true},
+};
+
+static int check_plan_choices() {
+  for (const Timed& t : kTimed) {
+    llmfa::FwdParams p{};
+    p.n_units = t.B * t.H * ((t.Sq + llmfa::kUnitRows - 1) / llmfa::kUnitRows);
+    p.n_kv = (t.Sk + llmfa::kBlockN - 1) / llmfa::kBlockN;
+    llmfa::make_plan(p, 74, true);
+    if ((p.sk_mode != 0) != t.sk_faster) {
+      std::printf("FAIL plan B%d H%d %dx%d: stream-K %d, measured faster %d\n", t.B, t.H, t.Sq,
+                  t.Sk, p.sk_mode, t.sk_faster ? 1 : 0);
+      return 1;
+    }
+    llmfa::FwdParams q{};  // without a workspace: always classic
+    q.n_units = p.n_units;
+    q.n_kv = p.n_kv;
+    llmfa::make_plan(q, 74, false);
+    if (q.sk_mode) return 1;
+  }
+  return 0;
+}
+
 int main() {
+  if (check_plan_choices()) return 1;
   int cases = 0;
   const int Gs[] = {1, 2, 3, 7, 74, 148};  // grids above kMaxSkParts are not planned
   for (int G : Gs)
