@@ -166,6 +166,7 @@ enum TraceEvent : int {
   kEvProdLoad,       // producer: V_j load issued (tile 0 slot) / K_{j+1} (tile 1 slot)
   kEvKVLanded,       // observer: V_j landed (tile 0 slot) / K_{j+1} landed (tile 1 slot)
   kEvMmaLoopTop,     // MMA: top of iteration j (tile 0) / QK_1(j+1) issued, not committed (tile 1)
+  kEvCorrPFull,      // correction: arrived on P full (its keys 96-127 written)
   kNumTraceEvents
 };
 struct TraceRecord {
@@ -764,6 +765,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
             ptx::tc_fence_before();
             __syncwarp();
             if (lane == 0) ptx::mbar_arrive_cluster(ptx::mapa(bar(kBarPFull + tile), 0));
+            if (warp == 8 && lane == 0) LLMFA_TRACE_EVENT(kEvCorrPFull, tile, j);
           }
         }
       }

@@ -18,11 +18,12 @@ from . import _lib
 
 EVENTS = ["s_ready", "ld_done", "stat", "p_half", "p_full", "mma_p_half", "mma_p_full",
           "mma_qk_next", "corr_stat", "corr_arrive", "mma_kv_ready", "prod_load", "kv_landed",
-          "mma_loop_top"]
+          "mma_loop_top", "corr_p_full"]
 ROLES = {"s_ready": "softmax", "ld_done": "softmax", "stat": "softmax", "p_half": "softmax",
          "p_full": "softmax", "mma_p_half": "mma", "mma_p_full": "mma", "mma_qk_next": "mma",
          "corr_stat": "correction", "corr_arrive": "correction", "mma_kv_ready": "mma",
-         "prod_load": "producer", "kv_landed": "producer", "mma_loop_top": "mma"}
+         "prod_load": "producer", "kv_landed": "producer", "mma_loop_top": "mma",
+         "corr_p_full": "correction"}
 TRACE_FIRST = 32
 TRACE_ITERS = 16
 RECORD = np.dtype([("globaltimer_ns", "<u8"), ("clock", "<i8")])
@@ -99,6 +100,8 @@ def hop_latencies(tr: np.ndarray, clock_ghz: float) -> dict[str, float]:
             out[k + "period (S visible to S visible)"] = np.median(np.diff(clk(r, t, "s_ready")))
             out[k + "correction sees rescale factor after it is published"] = np.median(
                 clk(r, t, "corr_stat") - clk(r, t, "stat"))
+            out[k + "correction P full - softmax P full (> 0: correction is later)"] = np.median(
+                clk(r, t, "corr_p_full") - clk(r, t, "p_full"))
     for t in (0, 1):
         k = f"tile{t}: "
         out[k + "cta0 P half -> MMA sees P half"] = np.median(clk(0, t, "mma_p_half") - clk(0, t, "p_half"))
