@@ -30,8 +30,9 @@
 //
 // The pair is persistent: cluster c processes units c, c + nclusters, ... in
 // (batch, head, query-block) order, so concurrently resident clusters share
-// K/V tiles in L2; with a workspace, the last partial wave of units is cut
-// into KV ranges across all clusters (stream-K, SegIter) and merged by
+// K/V tiles in L2; with a workspace, and where the planner's cost model
+// (make_plan) says it pays, the last partial wave of units is cut into KV
+// ranges across all clusters (stream-K, SegIter) and merged by
 // llm_fa_combine_kernel.
 //
 // No wait in this kernel is unbounded: every hand-off is an mbarrier, every
