@@ -246,11 +246,10 @@ def run_ours(args, cfg, world, rank, local):
     torch.cuda.synchronize(dev)
     if world > 1:
         dist.barrier()
-    # Keep the GPU behind the host: a short device-side sleep first, so every step's
-    # launches are queued before the GPU reaches them and no event interval contains
-    # host launch time (the Python call plus argument checks take tens of µs, about as
-    # long as the L2 flush before each step).
-    torch.cuda._sleep(int(2e6 + 2e5 * args.steps))
+    # Each step's 256 MiB flush runs ~70 µs on the GPU, longer than the host needs to
+    # queue the step's events and launches, so no event interval contains host time.
+    # (A device-side head start, tried instead, made the first steps slower: back to
+    # back flush + forward pairs without any idle gap.)
     for i in range(args.steps):
         flush.zero_()
         starts[i].record(stream)
@@ -335,9 +334,7 @@ def run_ours(args, cfg, world, rank, local):
                    "parallelism": {"all": "single GPU", "heads": f"heads sharded over {world} GPUs",
                                    "batch": f"batch sharded over {world} GPUs",
                                    "replica": f"{world} independent replicas"}[shard[0]],
-                   "l2": "flushed between timed steps (256 MiB write, outside the events)",
-                   "launch": "all timed steps queued before the GPU reaches them (device sleep "
-                             "first): the events time device work, not host launch gaps"},
+                   "l2": "flushed between timed steps (256 MiB write, outside the events)"},
         "roofline": {"bound": "tensor", "achieved": round(achieved, 2), "peak": peak,
                      "unit": "TFLOP/s", "frac": round(achieved / peak, 4),
                      "peak_source": peak_src,
