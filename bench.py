@@ -28,7 +28,6 @@ import os
 import statistics
 import subprocess
 import sys
-import threading
 import time
 from datetime import timedelta
 from pathlib import Path
@@ -86,7 +85,11 @@ def measured_peaks() -> dict:
 
 
 class ClockSampler:
-    """nvidia-smi samples (200 ms) of one GPU while the timed region runs."""
+    """nvidia-smi samples (200 ms) of one GPU while the timed region runs.
+
+    nvidia-smi writes its samples to a file (`-f`), read after the timed region: a
+    Python thread reading a pipe would take the interpreter lock during the timed
+    steps and delay their launches."""
 
     FIELDS = ("clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
               "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
@@ -96,23 +99,19 @@ class ClockSampler:
         self.index = index
         self.proc = None
         self.lines: list[str] = []
-        self.thread = None
+        self.path = None
 
     def start(self):
+        import tempfile
+        fd, self.path = tempfile.mkstemp(prefix="llmfa_clocks_", suffix=".csv")
+        os.close(fd)
         try:
             self.proc = subprocess.Popen(
                 ["nvidia-smi", f"--id={self.index}", f"--query-gpu={self.FIELDS}",
-                 "--format=csv,noheader,nounits", "-lms", "200"],
-                stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+                 "--format=csv,noheader,nounits", "-lms", "200", "-f", self.path],
+                stdout=subprocess.DEVNULL, stderr=subprocess.DEVNULL)
         except (OSError, ValueError):
             self.proc = None
-            return
-        self.thread = threading.Thread(target=self._read, daemon=True)
-        self.thread.start()
-
-    def _read(self):
-        for line in self.proc.stdout:
-            self.lines.append(line.strip())
 
     def stop(self) -> dict | None:
         if self.proc is None:
@@ -122,8 +121,12 @@ class ClockSampler:
             self.proc.wait(timeout=5)
         except subprocess.TimeoutExpired:
             self.proc.kill()
-        if self.thread is not None:
-            self.thread.join(timeout=2)
+        try:
+            with open(self.path) as f:
+                self.lines = [ln.strip() for ln in f]
+            os.unlink(self.path)
+        except OSError:
+            self.lines = []
         sm, mx, reasons = [], [], set()
         names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
         for ln in self.lines:
@@ -241,6 +244,11 @@ def run_ours(args, cfg, world, rank, local):
     sampler = ClockSampler(local)
     sampler.start()
     time.sleep(0.3)
+    # The GPU idled during the sleep and lowers its clocks meanwhile (the first step
+    # after it measured ~2x slower): the warm-up steps run again right before timing.
+    for _ in range(max(args.warmup, 3)):
+        flush.zero_()
+        step()
     starts = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
     ends = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
     torch.cuda.synchronize(dev)
@@ -248,8 +256,6 @@ def run_ours(args, cfg, world, rank, local):
         dist.barrier()
     # Each step's 256 MiB flush runs ~70 µs on the GPU, longer than the host needs to
     # queue the step's events and launches, so no event interval contains host time.
-    # (A device-side head start, tried instead, made the first steps slower: back to
-    # back flush + forward pairs without any idle gap.)
     for i in range(args.steps):
         flush.zero_()
         starts[i].record(stream)
@@ -399,14 +405,20 @@ def run_reference(args, cfg, world, rank, local):
         for Q, K, V in per_head:
             mod.llm_fa_forward(Q, K, V)
     torch.cuda.synchronize()
+    n_warm = max(args.warmup, 3)
     with profile(activities=[ProfilerActivity.CUDA]) as prof:
-        for _ in range(args.steps):
+        # warm-up launches again inside the profiled region (the GPU may have lowered
+        # its clocks while the profiler started); only the last steps' launches count
+        for _ in range(n_warm + args.steps):
             flush.zero_()
             for Q, K, V in per_head:
                 mod.llm_fa_forward(Q, K, V)
         torch.cuda.synchronize()
-    durs = [e.device_time_total for e in prof.events()
-            if "llm_fa_kernel" in e.name and e.device_type == torch.autograd.DeviceType.CUDA]
+    kern = sorted((e for e in prof.events()
+                   if "llm_fa_kernel" in e.name
+                   and e.device_type == torch.autograd.DeviceType.CUDA),
+                  key=lambda e: e.time_range.start)
+    durs = [e.device_time_total for e in kern][n_warm * len(per_head):]
     total_us = sum(durs)
     step_ms = total_us / 1e3 / args.steps
     value = cfg.flops / (step_ms / 1e3) / 1e12
