@@ -1,29 +1,34 @@
 #!/usr/bin/env python
 """Attention-forward benchmark (bf16, head dim 128, non-causal) on B200.
 
-    python bench.py [--gpus N] [--steps K] [--warmup W] [--config c2] [--impl ours|reference]
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--config c3] [--impl ours|reference]
 
 One step = one forward over the configuration's inputs, already resident in
 HBM. Each timed launch is bracketed by CUDA events on the launching stream;
 L2 (126 MB) is flushed by a 256 MiB write between timed steps, outside the
 events. value = algorithmic FLOPs (4*B*H*Sq*Sk*128) of all ranks / the
-slowest rank's mean step time. With N > 1 ranks (torchrun, one per GPU):
-configurations with several heads are sharded over heads (no exchange in the
-data path; NCCL only gathers O afterwards when --validate is given); single
-(batch, head) configurations run one replica per GPU.
+slowest rank's mean step time.
+
+With N > 1 ranks (torchrun, one per GPU, NCCL) every rank runs an
+exchange-free shard of the configuration: its heads when the head count
+divides by N, else its batch entries, else a contiguous block of query rows
+(rows of one head are independent; every rank holds all of K and V), else a
+replica. The data path has no collective; NCCL only takes the max of the
+ranks' times and, with --validate, gathers O afterwards.
 
 `--impl reference` times the reference's own kernel (llm_fa.cu built from its
-sources into oracle/_ref/) through its own `llm_fa_forward` on rank 0, one 2-D
-launch per (batch, head), kernel durations from CUPTI (the reference launcher
-allocates O and synchronises the device inside every call, so events on the
-stream cannot bracket its kernel alone); when that module is absent it times
-the reference's CPU oracle path (fp32 SDPA, validate.py:19-27) instead.
+sources into oracle/_ref/) through its own `llm_fa_forward`, one 2-D launch per
+(batch, head), on every rank with the same shard as this arm; kernel durations
+come from CUPTI (the reference launcher allocates O and synchronises the
+device inside every call, so stream events cannot bracket its kernel alone).
+Its `e2e` takes the same host-data path as this arm's: pinned Q/K/V copied in,
+the call, O copied back, every step. When that module is absent it times the
+reference's CPU oracle path (fp32 SDPA, validate.py:19-27) instead.
 """
 from __future__ import annotations
 
 import argparse
 import json
-import math
 import os
 import statistics
 import subprocess
@@ -37,14 +42,19 @@ sys.path.insert(0, str(ROOT))
 
 METRIC = "attn fwd TFLOP/s bf16 hd128 & % of tensor peak; µs vs llm_fa.cu/FA4 same box"
 UNIT = "TFLOP/s"
-# Reference's published TFLOP/s for the same shapes (ncu, SM clock locked
-# at ~1.07 GHz, computed from the published microseconds of llm_fa.cu).
+DATA = "synthetic (seeded N(0,1) bf16 inputs at the BASELINE.json shapes, drawn on the CPU)"
+# The reference's published TFLOP/s for two of the configurations, computed from its
+# published kernel microseconds (llm_fa.cu at 16384^2 and 32768x131072), which were measured
+# under ncu with the SM clock locked near 1.07 GHz: not comparable with CUDA-event timings
+# at the default clock, so they are reported beside the line and vs_baseline stays null.
 PUBLISHED_REF_TFLOPS = {"c2": 362.5, "c3": 810.6}
-# DRAM bytes per launch (dram__bytes_read.sum + dram__bytes_write.sum) from the ncu capture
-# summarised in profiles/; None until measured for that configuration.
+# DRAM bytes (dram__bytes_read.sum + dram__bytes_write.sum) of one launch of the attention
+# kernel at this configuration, from an ncu capture of the current kernel: a profile-time
+# figure (ncu replays each launch with cold caches, and O's writes can stay in L2 when the
+# kernel ends), not a measurement of the timed steps.
 PROFILED_TRAFFIC_BYTES: dict[str, float | None] = {
-    "c2": 12.66e6,   # profiles/llm_fa_kernel_c2_ncu.md
-    "c3": 142.6e6,   # profiles/llm_fa_kernel_c3_ncu.md
+    "c2": 12.66e6,
+    "c3": 142.6e6,
 }
 L2_FLUSH_BYTES = 256 << 20
 
@@ -54,15 +64,15 @@ def parse_args():
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=20)
     ap.add_argument("--warmup", type=int, default=5)
-    ap.add_argument("--config", default="c2", help="c1..c5 (BASELINE.json configs)")
+    ap.add_argument("--config", default="c3", help="c1..c5 (BASELINE.json configs)")
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--validate", action="store_true", help="NCCL-gather O to rank 0 afterwards")
     ap.add_argument("--cpu-seconds", type=float, default=10.0, help="CPU baseline sample budget")
     ap.add_argument("--sweep", action="store_true",
-                    help="time this kernel and the reference kernel on the reference's eight "
-                         "published single-head shapes (one JSON line per shape)")
+                    help="time this kernel and the reference kernel on the reference's published "
+                         "single-head shapes and on multi-wave ones (one JSON line per shape)")
     return ap.parse_args()
 
 
@@ -149,8 +159,8 @@ class ClockSampler:
 
 # ------------------------------------------------------------------ workload
 def local_shard(cfg, world: int, rank: int):
-    """Which part of the workload this rank runs: ('heads', h0, h1), ('batch', b0, b1) or
-    ('replica',)."""
+    """This rank's exchange-free part of the workload: ('all',), ('heads', h0, h1),
+    ('batch', b0, b1), ('rows', s0, s1) (query rows; K and V whole) or ('replica',)."""
     if world == 1:
         return ("all",)
     if cfg.heads % world == 0:
@@ -159,6 +169,9 @@ def local_shard(cfg, world: int, rank: int):
     if cfg.batch % world == 0:
         bs = cfg.batch // world
         return ("batch", rank * bs, (rank + 1) * bs)
+    if cfg.seq_q % (512 * world) == 0:  # whole 512-row query blocks per rank
+        rs = cfg.seq_q // world
+        return ("rows", rank * rs, (rank + 1) * rs)
     return ("replica",)
 
 
@@ -167,11 +180,28 @@ def slice_inputs(q, k, v, shard):
         return tuple(t[:, :, shard[1]:shard[2]].contiguous() for t in (q, k, v))
     if shard[0] == "batch":
         return tuple(t[shard[1]:shard[2]].contiguous() for t in (q, k, v))
+    if shard[0] == "rows":
+        return q[:, shard[1]:shard[2]].contiguous(), k, v
     return q, k, v
 
 
+def parallelism(shard, world: int) -> str:
+    return {"all": "single GPU", "heads": f"heads sharded over {world} GPUs",
+            "batch": f"batch sharded over {world} GPUs",
+            "rows": f"query rows sharded over {world} GPUs (K/V on every GPU)",
+            "replica": f"{world} independent replicas"}[shard[0]]
+
+
+def config_dict(cfg, shard, world: int) -> dict:
+    """The `config` object of both arms' lines (identical for the same run)."""
+    return {"workload": f"{cfg.name}: {cfg.describe()} non-causal, scale 1/sqrt(128)",
+            "global_batch": cfg.batch, "heads": cfg.heads, "seq_q": cfg.seq_q,
+            "seq_k": cfg.seq_k, "head_dim": 128, "parallelism": parallelism(shard, world),
+            "l2": "flushed between timed steps (256 MiB write, outside the timed kernels)"}
+
+
 def cpu_baseline(cfg, budget_s: float) -> dict:
-    """The reference's oracle path (fp32 SDPA, validate.py:19-27) on host cores, on a
+    """The reference's oracle path (fp32 SDPA, validate.py:19-27) on all host cores, on a
     seeded subset of query rows of one head (rows are independent)."""
     import torch
 
@@ -205,8 +235,56 @@ def cpu_baseline(cfg, budget_s: float) -> dict:
     t = total / reps
     flops = 4.0 * len(rows) * cfg.seq_k * 128
     return {"value": flops / t / 1e12, "unit": UNIT, "cores": threads, "kind": "port",
-            "sample": f"fp32 SDPA (torch CPU) on {len(rows)} seeded query rows x {cfg.seq_k} keys "
-                      f"of one head, {reps} reps, {t:.2f} s/rep; TFLOP/s of that sample"}
+            "sample": f"fp32 SDPA (torch CPU, the reference's oracle path) on {len(rows)} seeded "
+                      f"query rows x {cfg.seq_k} keys of one head, {reps} reps, {t:.2f} s/rep; "
+                      "TFLOP/s of that sample"}
+
+
+def copy_bandwidth(host_in, host_out, dev) -> dict:
+    """Pinned-memory copy rates of this box for the step's own buffers: all inputs
+    host-to-device, then the output device-to-host, each alone on one stream (best of 3,
+    CUDA events). These bound a host-data step from below."""
+    import torch
+    dev_in = [torch.empty(t.shape, dtype=t.dtype, device=dev) for t in host_in]
+    dev_out = torch.empty(host_out.shape, dtype=host_out.dtype, device=dev)
+    n_in = sum(t.numel() * t.element_size() for t in host_in)
+    n_out = host_out.numel() * host_out.element_size()
+    best_in, best_out = float("inf"), float("inf")
+    for _ in range(3):
+        e = [torch.cuda.Event(enable_timing=True) for _ in range(3)]
+        e[0].record()
+        for d, h in zip(dev_in, host_in):
+            d.copy_(h, non_blocking=True)
+        e[1].record()
+        host_out.copy_(dev_out, non_blocking=True)
+        e[2].record()
+        torch.cuda.synchronize(dev)
+        best_in = min(best_in, e[0].elapsed_time(e[1]))
+        best_out = min(best_out, e[1].elapsed_time(e[2]))
+    return {"h2d_gbs": round(n_in / best_in / 1e6, 2), "d2h_gbs": round(n_out / best_out / 1e6, 2),
+            "h2d_ms": best_in, "d2h_ms": best_out}
+
+
+def max_over_ranks(values: list[float], dev) -> list[float]:
+    import torch
+    import torch.distributed as dist
+    t = torch.tensor(values, dtype=torch.float64, device=dev)
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return [float(x) for x in t]
+
+
+def gather_floats(value: float, dev) -> list[float]:
+    import torch
+    import torch.distributed as dist
+    t = torch.tensor([value], dtype=torch.float64, device=dev)
+    parts = [torch.empty_like(t) for _ in range(dist.get_world_size())]
+    dist.all_gather(parts, t)
+    return [float(p[0]) for p in parts]
+
+
+def clocks_from_samplers(*clocks):
+    got = [c for c in clocks if c]
+    return got[0] if got else None
 
 
 # ------------------------------------------------------------------ our arm
@@ -214,9 +292,13 @@ def run_ours(args, cfg, world, rank, local):
     import torch
     import torch.distributed as dist
 
-    from llm_fa_b200 import attention_forward, device_status, launch_plan
+    from llm_fa_b200 import attention_forward, build_info, device_status, launch_plan
     from llm_fa_b200.workloads import make_inputs
 
+    info = build_info()
+    if info["ablation"] != 0:
+        raise RuntimeError(f"library built with ablation switch {info['ablation_name']!r}: "
+                           "its output is not attention; it is not timed as the product")
     torch.cuda.set_device(local)
     dev = torch.device("cuda", local)
     shard = local_shard(cfg, world, rank)
@@ -279,6 +361,7 @@ def run_ours(args, cfg, world, rank, local):
         from llm_fa_b200.host import HostAttention
         qp, kp, vp = (t.contiguous().pin_memory() for t in (q_h, k_h, v_h))
         op = torch.empty(qp.shape, dtype=qp.dtype).pin_memory()
+        bw = copy_bandwidth([qp, kp, vp], op, dev)
         ha = HostAttention(dev, depth=2)
         for _ in range(max(args.warmup, 3)):
             ha.submit(qp, kp, vp, op)
@@ -294,16 +377,13 @@ def run_ours(args, cfg, world, rank, local):
         torch.cuda.synchronize(dev)
         e2e_ms = e_start.elapsed_time(e_end) / args.steps
         e2e = {"ms": e2e_ms, "h2d": sum(t.numel() * t.element_size() for t in (q_h, k_h, v_h)),
-               "d2h": o.numel() * o.element_size()}
+               "d2h": o.numel() * o.element_size(), "bw": bw}
 
     # max over ranks
     if world > 1:
-        t = torch.tensor([mean_ms, e2e["ms"] if e2e else 0.0], dtype=torch.float64, device=dev)
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        mean_ms_max, e2e_ms_max = float(t[0]), float(t[1])
-        tot = torch.tensor([float(flops_local)], dtype=torch.float64, device=dev)
-        dist.all_reduce(tot)
-        flops_total = float(tot[0])
+        mean_ms_max, e2e_ms_max = max_over_ranks([mean_ms, e2e["ms"] if e2e else 0.0], dev)
+        per_rank_ms = gather_floats(mean_ms, dev)
+        flops_total = float(flops_local) * world if shard[0] != "all" else float(flops_local)
         if args.validate:
             gathered = [torch.empty_like(o) for _ in range(world)]
             dist.all_gather(gathered, o)
@@ -313,6 +393,7 @@ def run_ours(args, cfg, world, rank, local):
     else:
         mean_ms_max = mean_ms
         e2e_ms_max = e2e["ms"] if e2e else 0.0
+        per_rank_ms = [mean_ms]
         flops_total = float(flops_local)
 
     if rank != 0:
@@ -321,7 +402,8 @@ def run_ours(args, cfg, world, rank, local):
     peak = peaks.get("bf16_tflops")
     peak_src = "measured burst (MEASURED_PEAKS.json bf16_tflops)" if peak else "fallback 1590"
     peak = float(peak) if peak else 1590.0
-    achieved = flops_local / (mean_ms / 1e3) / 1e12  # this rank's kernel, per launch
+    peak_sus = float(peaks.get("bf16_tflops_sustained") or 1400.0)
+    achieved = flops_local / (mean_ms / 1e3) / 1e12  # this rank's kernels, per forward
     value = flops_total / (mean_ms_max / 1e3) / 1e12
     line = {
         "metric": METRIC, "value": round(value, 2), "unit": UNIT, "n_gpus": world,
@@ -330,34 +412,48 @@ def run_ours(args, cfg, world, rank, local):
         "ms_per_step_median": round(statistics.median(times_ms), 5),
         "ms_per_step_min": round(min(times_ms), 5),
         "higher_is_better": True,
-        "scaling": "strong" if shard[0] in ("heads", "batch") else "weak",
-        "vs_baseline": (round(value / world / PUBLISHED_REF_TFLOPS[cfg.name], 3)
-                        if cfg.name in PUBLISHED_REF_TFLOPS else None),
-        "dtype": "bf16", "data": "synthetic (seeded N(0,1) bf16 inputs, BASELINE.json shapes)",
-        "config": {"workload": f"{cfg.name}: {cfg.describe()} non-causal, scale 1/sqrt(128)",
-                   "global_batch": cfg.batch, "heads": cfg.heads, "seq_q": cfg.seq_q,
-                   "seq_k": cfg.seq_k, "head_dim": 128,
-                   "parallelism": {"all": "single GPU", "heads": f"heads sharded over {world} GPUs",
-                                   "batch": f"batch sharded over {world} GPUs",
-                                   "replica": f"{world} independent replicas"}[shard[0]],
-                   "l2": "flushed between timed steps (256 MiB write, outside the events)"},
+        "scaling": "strong" if shard[0] in ("heads", "batch", "rows") else "weak",
+        "vs_baseline": None,
+        "dtype": "bf16", "data": DATA,
+        "config": config_dict(cfg, shard, world),
         "roofline": {"bound": "tensor", "achieved": round(achieved, 2), "peak": peak,
                      "unit": "TFLOP/s", "frac": round(achieved / peak, 4),
                      "peak_source": peak_src,
-                     "traffic": PROFILED_TRAFFIC_BYTES.get(cfg.name),
-                     "algorithmic_bytes": cfg.io_bytes},
+                     "peak_sustained": peak_sus,
+                     "frac_of_sustained": round(achieved / peak_sus, 4),
+                     "traffic": PROFILED_TRAFFIC_BYTES.get(cfg.name) if shard[0] == "all" else None,
+                     "traffic_source": ("ncu dram__bytes_read.sum + dram__bytes_write.sum of one "
+                                        "attention-kernel launch at this configuration (profile "
+                                        "time, cold caches; O writes may stay in L2)"),
+                     "algorithmic_bytes": 2 * 128 * B * H * (2 * Sq + 2 * Sk)},
         "gpu_launches": args.steps * plan["kernels"],
         "launch_plan": plan,
         "clocks": clocks,
     }
+    if world > 1:
+        line["per_rank_ms"] = [round(x, 5) for x in per_rank_ms]
+    if cfg.name in PUBLISHED_REF_TFLOPS:
+        line["published_reference"] = {
+            "value": PUBLISHED_REF_TFLOPS[cfg.name], "unit": UNIT,
+            "conditions": "reference's published llm_fa.cu time: ncu, SM clock locked near "
+                          "1.07 GHz; not comparable with this line (CUDA events, default "
+                          "clocks); the same-box reference arm is the comparison"}
     if e2e is not None:
-        line["e2e"] = {"value": round(flops_total / (e2e_ms_max / 1e3) / 1e12, 2), "unit": UNIT,
+        e2e_value = flops_total / (e2e_ms_max / 1e3) / 1e12
+        bound_ms = max(e2e["bw"]["h2d_ms"], e2e["bw"]["d2h_ms"], mean_ms)
+        line["e2e"] = {"value": round(e2e_value, 2), "unit": UNIT,
                        "h2d_bytes_per_step": e2e["h2d"], "d2h_bytes_per_step": e2e["d2h"],
                        "ms_per_step": round(e2e_ms_max, 4),
                        "pipeline_depth": 2,
                        "path": ("llm_fa_b200.host.HostAttention: pinned host Q/K/V in, O out, "
                                 "every step; copies of neighbouring steps overlap compute; "
-                                "device-timed over all steps / steps")}
+                                "device-timed over all steps / steps"),
+                       # the step can go no faster than its slowest stage: all inputs in at the
+                       # box's pinned copy rate, the output out, or the kernels
+                       "copy_roofline": {"h2d_gbs": e2e["bw"]["h2d_gbs"],
+                                         "d2h_gbs": e2e["bw"]["d2h_gbs"],
+                                         "bound_ms": round(bound_ms, 4),
+                                         "frac": round(bound_ms / e2e_ms_max, 4)}}
         line["gpu_launches"] += args.steps * plan["kernels"]
     if world == 1 and not args.no_cpu_baseline:
         line["cpu_baseline"] = cpu_baseline(cfg, args.cpu_seconds)
@@ -366,13 +462,10 @@ def run_ours(args, cfg, world, rank, local):
 
 # ------------------------------------------------------------------ reference arm
 def run_reference(args, cfg, world, rank, local):
-    if rank != 0:
-        return None
+    import torch
     line = {"metric": METRIC, "unit": UNIT, "n_gpus": world, "steps": args.steps,
             "warmup": args.warmup, "higher_is_better": True, "impl": "reference",
-            "dtype": "bf16", "data": "synthetic (seeded N(0,1) bf16 inputs, BASELINE.json shapes)",
-            "vs_baseline": None}
-    import torch
+            "dtype": "bf16", "data": DATA, "vs_baseline": None}
     mod = None
     try:
         from oracle.build_ref import load_module
@@ -381,12 +474,14 @@ def run_reference(args, cfg, world, rank, local):
     except Exception as exc:  # fall back to the CPU oracle path
         print(f"# reference kernel unavailable ({exc}); timing the CPU oracle path",
               file=sys.stderr)
-    cpu = cpu_baseline(cfg, args.cpu_seconds)
     if mod is None:
+        if rank != 0:
+            return None
+        cpu = cpu_baseline(cfg, args.cpu_seconds)
         line.update({"value": round(cpu["value"], 6), "scaling": "weak",
                      "ms_per_step": None, "cpu_baseline": cpu,
-                     "config": {"workload": f"{cfg.name}: {cfg.describe()}",
-                                "parallelism": "CPU, all host threads"},
+                     "config": dict(config_dict(cfg, ("all",), 1),
+                                    parallelism="CPU, all host threads"),
                      "e2e": {"value": round(cpu["value"], 6), "unit": UNIT,
                              "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}})
         return line
@@ -395,17 +490,27 @@ def run_reference(args, cfg, world, rank, local):
     from llm_fa_b200.workloads import make_inputs
     torch.cuda.set_device(local)
     dev = torch.device("cuda", local)
-    q, k, v = make_inputs(cfg)
+    shard = local_shard(cfg, world, rank)
+    q, k, v = slice_inputs(*make_inputs(cfg), shard)
+    B, Sq, H, _ = q.shape
+    Sk = k.shape[1]
+    flops_local = 4 * B * H * Sq * Sk * 128
     # the reference takes 2-D (q,128)/(sk,128) contiguous tensors: one launch per (b, h)
-    heads = [(b, h) for b in range(cfg.batch) for h in range(cfg.heads)]
-    per_head = [(q[b, :, h].contiguous().to(dev), k[b, :, h].contiguous().to(dev),
-                 v[b, :, h].contiguous().to(dev)) for b, h in heads]
+    heads = [(b, h) for b in range(B) for h in range(H)]
+    per_head_host = [(q[b, :, h].contiguous(), k[b, :, h].contiguous(), v[b, :, h].contiguous())
+                     for b, h in heads]
+    per_head = [tuple(t.to(dev) for t in x) for x in per_head_host]
     flush = torch.empty(L2_FLUSH_BYTES, dtype=torch.uint8, device=dev)
     for _ in range(max(args.warmup, 3)):
         for Q, K, V in per_head:
             mod.llm_fa_forward(Q, K, V)
     torch.cuda.synchronize()
+    if world > 1:
+        import torch.distributed as dist
+        dist.barrier()
     n_warm = max(args.warmup, 3)
+    sampler = ClockSampler(local)
+    sampler.start()
     with profile(activities=[ProfilerActivity.CUDA]) as prof:
         # warm-up launches again inside the profiled region (the GPU may have lowered
         # its clocks while the profiler started); only the last steps' launches count
@@ -414,46 +519,95 @@ def run_reference(args, cfg, world, rank, local):
             for Q, K, V in per_head:
                 mod.llm_fa_forward(Q, K, V)
         torch.cuda.synchronize()
+    clocks = sampler.stop()
     kern = sorted((e for e in prof.events()
                    if "llm_fa_kernel" in e.name
                    and e.device_type == torch.autograd.DeviceType.CUDA),
                   key=lambda e: e.time_range.start)
     durs = [e.device_time_total for e in kern][n_warm * len(per_head):]
-    total_us = sum(durs)
-    step_ms = total_us / 1e3 / args.steps
-    value = cfg.flops / (step_ms / 1e3) / 1e12
+    step_ms = sum(durs) / 1e3 / args.steps
+
+    # end to end, the host-data path a caller of the reference takes: per step, copy each
+    # head's Q, K, V in from pinned host memory, call llm_fa_forward (it allocates O and
+    # synchronises the device), copy O back to pinned host memory; CUDA events on the
+    # stream all of it runs on (the legacy default stream)
+    e2e = None
+    if not args.no_e2e:
+        pinned = [tuple(t.pin_memory() for t in x) for x in per_head_host]
+        o_pinned = [torch.empty(x[0].shape, dtype=torch.bfloat16).pin_memory() for x in pinned]
+        dev_in = [tuple(torch.empty_like(t, device=dev) for t in x) for x in pinned]
+
+        def host_step():
+            for (qh, kh, vh), (qd, kd, vd), oh in zip(pinned, dev_in, o_pinned):
+                qd.copy_(qh, non_blocking=True)
+                kd.copy_(kh, non_blocking=True)
+                vd.copy_(vh, non_blocking=True)
+                oh.copy_(mod.llm_fa_forward(qd, kd, vd)[0], non_blocking=True)
+
+        for _ in range(max(args.warmup, 3)):
+            host_step()
+        torch.cuda.synchronize()
+        if world > 1:
+            dist.barrier()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for _ in range(args.steps):
+            host_step()
+        e1.record()
+        torch.cuda.synchronize()
+        e2e = {"ms": e0.elapsed_time(e1) / args.steps,
+               "h2d": sum(t.numel() * t.element_size() for x in pinned for t in x),
+               "d2h": sum(t.numel() * t.element_size() for t in o_pinned)}
+
+    if world > 1:
+        step_ms_max, e2e_ms_max = max_over_ranks([step_ms, e2e["ms"] if e2e else 0.0], dev)
+        per_rank_ms = gather_floats(step_ms, dev)
+        flops_total = float(flops_local) * world
+    else:
+        step_ms_max, e2e_ms_max, per_rank_ms = step_ms, (e2e["ms"] if e2e else 0.0), [step_ms]
+        flops_total = float(flops_local)
+    if rank != 0:
+        return None
+    value = flops_total / (step_ms_max / 1e3) / 1e12
     line.update({
-        "value": round(value, 2), "ms_per_step": round(step_ms, 5), "scaling": "weak",
-        "config": {"workload": f"{cfg.name}: {cfg.describe()} non-causal",
-                   "parallelism": "single GPU, one 2-D launch per (batch, head)",
-                   "l2": "flushed between timed steps (256 MiB write)",
-                   "timing": f"CUPTI kernel durations of {len(durs)} llm_fa_kernel launches"},
-        "kernel_us_per_launch": round(total_us / max(len(durs), 1), 2),
+        "value": round(value, 2), "ms_per_step": round(step_ms_max, 5),
+        "scaling": "strong" if shard[0] in ("heads", "batch", "rows") else "weak",
+        "config": config_dict(cfg, shard, world),
+        "reference_kernel": {
+            "value": round(value, 2), "unit": UNIT,
+            "kernel_us_per_launch": round(sum(durs) / max(len(durs), 1), 2),
+            "launches_per_step": len(heads),
+            "timing": (f"CUPTI kernel durations of {len(durs)} llm_fa_kernel launches "
+                       "(oracle/_ref: the reference's llm_fa.cu built from its sources), one 2-D "
+                       "launch per (batch, head)")},
         "gpu_launches": len(durs),
-        # this run: the reference's own implementation of the path (its llm_fa.cu kernel,
-        # compiled from the reference sources; it has no CPU implementation of the path)
-        "cpu_baseline": {"value": round(value, 2), "unit": UNIT, "cores": 1, "kind": "reference",
-                         "sample": (f"reference llm_fa_kernel (oracle/_ref), {args.steps} steps of "
-                                    f"{len(heads)} launches, whole workload; launched from one "
-                                    "host thread")},
-        "cpu_oracle": cpu,  # the reference's CPU oracle path (fp32 SDPA), for context
-        "e2e": {"value": round(value, 2), "unit": UNIT, "h2d_bytes_per_step": 0,
-                "d2h_bytes_per_step": 0},
+        "clocks": clocks,
     })
+    if world > 1:
+        line["per_rank_ms"] = [round(x, 5) for x in per_rank_ms]
+    if e2e is not None:
+        line["e2e"] = {"value": round(flops_total / (e2e_ms_max / 1e3) / 1e12, 2), "unit": UNIT,
+                       "h2d_bytes_per_step": e2e["h2d"], "d2h_bytes_per_step": e2e["d2h"],
+                       "ms_per_step": round(e2e_ms_max, 4),
+                       "path": ("reference llm_fa_forward per (batch, head): pinned host Q/K/V "
+                                "copied in, the call (allocates O, synchronises the device), O "
+                                "copied out, every step; CUDA events around all steps")}
+    if not args.no_cpu_baseline:
+        line["cpu_baseline"] = cpu_baseline(cfg, args.cpu_seconds)
     return line
 
 
-# The reference's published single-head shapes (q, sk), README.md:58-65 of the reference.
-SWEEP_SHAPES = [(q, sk) for q in (16384, 32768) for sk in (16384, 32768, 65536, 131072)]
+# The reference's published single-head shapes (q, sk) (its README's latency table), and
+# multi-wave ones (q > 32768: the reference launches more 512-row clusters than fit at once).
+SWEEP_SHAPES = [(q, sk) for q in (16384, 32768) for sk in (16384, 32768, 65536, 131072)] + [
+    (65536, 16384), (65536, 131072), (131072, 32768)]
 
 
 def run_sweep(args) -> None:
     """This kernel and the reference's llm_fa.cu kernel (oracle/_ref) on the same GPU, on
-    the reference's published shapes: CUDA events around each call, a 256 MiB L2 flush
-    before every call, median of --steps calls after --warmup; also the largest
-    difference between the two outputs."""
-    import statistics
-
+    the sweep shapes: CUDA events around each call, a 256 MiB L2 flush before every call,
+    median of --steps calls after --warmup; also the largest difference between the two
+    outputs."""
     import torch
 
     from llm_fa_b200 import attention_forward, device_status
@@ -491,6 +645,7 @@ def run_sweep(args) -> None:
                           "ours_tflops": round(flops / t_ours / 1e6, 1),
                           "reference_tflops": round(flops / t_ref / 1e6, 1),
                           "max_abs_diff_vs_reference": diff}), flush=True)
+        del Q, K, V, O
     if device_status() != 0:
         raise RuntimeError(f"device status {device_status()}")
 
@@ -506,11 +661,6 @@ def main():
               file=sys.stderr)
     from llm_fa_b200.workloads import CONFIGS
     cfg = CONFIGS[args.config]
-    if args.impl == "reference":
-        line = run_reference(args, cfg, world, rank, local)
-        if line is not None:
-            print(json.dumps(line), flush=True)
-        return
     import torch.distributed as dist
     if world > 1:
         import torch
@@ -518,7 +668,8 @@ def main():
         dist.init_process_group("nccl", timeout=timedelta(seconds=300),
                                 device_id=torch.device("cuda", local))
     try:
-        line = run_ours(args, cfg, world, rank, local)
+        run = run_reference if args.impl == "reference" else run_ours
+        line = run(args, cfg, world, rank, local)
     finally:
         if world > 1:
             dist.destroy_process_group()

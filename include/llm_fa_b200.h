@@ -122,12 +122,27 @@ const char* llmfa_error_string(int status);
 int llmfa_version(void);
 
 /*
+ * Compile-time configuration of this library build: `*ablation` = the
+ * ablation-ladder rung (0 = the product; 1 = TMA + MMA floor, 2 = no softmax
+ * math, 3 = no exponentials: the output of rungs 1-3 is not attention) and
+ * `*trace` = 1 when built with the event trace (-DLLMFA_TRACE=1). Replaces
+ * the reference's separate ladder kernels (scaffolding.cu with SKIP_SM_FULL,
+ * faux.cu) and its ENABLE_PROF build flag (llm_fa.py:46-51), which it reports
+ * nowhere at run time.
+ */
+int llmfa_build_config(int* ablation, int* trace);
+
+/*
  * Event trace of the last launch (library built with -DLLMFA_TRACE=1 only;
  * otherwise returns LLMFA_ERR_UNSUPPORTED): copies the trace records
  * ({uint64 globaltimer_ns, int64 clock64} per [cta rank][Q tile][event]
  * [iteration]) to host memory after synchronising the device, followed, when
  * `capacity_bytes` allows, by the per-cluster segment timeline (uint64
- * [160 clusters][32 segments][4]). Replaces the reference's
+ * [160 clusters][32 segments][4]) and then by the per-wait-site statistics
+ * of every launch since the last read (uint64 [16][2]: entry 0 = summed CTA
+ * run time in SM cycles and the CTA count; entry s = %clock64 cycles lane 0 of
+ * the waiting warps spent in the bounded waits of site s and their number),
+ * which the read clears. Replaces the reference's
  * profiler ring flush (profiler.cuh:85-108) and the prof_buf / prof_count
  * outputs of llm_fa_forward (llm_fa.cu:1461-1474).
  */
@@ -142,9 +157,11 @@ int llmfa_trace_read(void* dst_host, uint64_t capacity_bytes, uint64_t* written_
  * library (148 partial-result slots: two per 2-SM cluster of a 148-SM B200),
  * which every GPU that loads the library keeps until the process exits.
  * Returns LLMFA_ERR_UNSUPPORTED on a device that would need more slots than
- * that. The first call on each device looks up the array's device address
- * (cudaGetSymbolAddress, with that device current); make that first call
- * before any stream capture. All calls share the one array, so calls that
+ * that (more than 74 two-SM clusters resident), for every shape, including
+ * shapes that would not split any KV range. Arguments are checked as for
+ * llmfa_forward before any CUDA call. The first call on each device looks up
+ * the array's device address (cudaGetSymbolAddress, with that device
+ * current); make that first call before any stream capture. All calls share the one array, so calls that
  * overlap on the GPU (other streams, other host threads) race on it and must
  * be serialised by the caller. The array's contents from the last call are
  * left in place; nothing in it has to start at zero. Other arguments and

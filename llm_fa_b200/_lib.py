@@ -57,6 +57,8 @@ SIGNATURES = {
                                          ctypes.POINTER(ctypes.c_int)]),
     "llmfa_error_string": (ctypes.c_char_p, [ctypes.c_int]),
     "llmfa_version": (ctypes.c_int, []),
+    "llmfa_build_config": (ctypes.c_int, [ctypes.POINTER(ctypes.c_int),
+                                          ctypes.POINTER(ctypes.c_int)]),
     "llmfa_selftest_wait_timeout": (ctypes.c_int, [ctypes.c_uint32, ctypes.c_void_p]),
     "llmfa_trace_read": (ctypes.c_int, [ctypes.c_void_p, ctypes.c_uint64,
                                         ctypes.POINTER(ctypes.c_uint64)]),
@@ -71,23 +73,41 @@ class LlmfaError(RuntimeError):
         super().__init__(f"{what}: {error_string(code)} (status {code})")
 
 
+def load(path: Path | str) -> ctypes.CDLL:
+    """Load one build of the library (the product, or a trace/ablation variant built by
+    llm_fa_b200.build.build_variant) as its own handle, with every signature set."""
+    path = Path(path)
+    if not path.exists():
+        raise ImportError(f"{path.name} is not built; run `python -m llm_fa_b200.build` "
+                          "(there is no non-CUDA fallback)")
+    handle = ctypes.CDLL(str(path), mode=os.RTLD_NOW | os.RTLD_LOCAL)
+    for name, (res, args) in SIGNATURES.items():
+        fn = getattr(handle, name)
+        fn.restype = res
+        fn.argtypes = args
+    return handle
+
+
 def lib() -> ctypes.CDLL:
-    """Load the shared library once; raise if it is not there."""
+    """Load the product library once; raise if it is not there."""
     global _lib
     if _lib is None:
         with _lock:
             if _lib is None:
-                if not LIB_PATH.exists():
-                    raise ImportError(
-                        f"{LIB_PATH.name} is not built; run `python -m llm_fa_b200.build` "
-                        "(there is no non-CUDA fallback)")
-                handle = ctypes.CDLL(str(LIB_PATH), mode=os.RTLD_NOW | os.RTLD_LOCAL)
-                for name, (res, args) in SIGNATURES.items():
-                    fn = getattr(handle, name)
-                    fn.restype = res
-                    fn.argtypes = args
-                _lib = handle
+                _lib = load(LIB_PATH)
     return _lib
+
+
+ABLATION_NAMES = {0: "none", 1: "floor", 2: "faux", 3: "noexp"}
+
+
+def build_config(handle: ctypes.CDLL | None = None) -> dict:
+    """Compile-time configuration of a library build (llmfa_build_config)."""
+    h = lib() if handle is None else handle
+    a, t = ctypes.c_int(-1), ctypes.c_int(-1)
+    check(h.llmfa_build_config(ctypes.byref(a), ctypes.byref(t)), "llmfa_build_config")
+    return {"ablation": a.value, "ablation_name": ABLATION_NAMES.get(a.value, str(a.value)),
+            "trace": bool(t.value)}
 
 
 def error_string(code: int) -> str:

@@ -52,6 +52,16 @@ def attention_forward(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, *,
     2-D ones (llmfa_forward_lse). Raises RuntimeError on invalid input or a
     nonzero library status.
     """
+    return forward_with(_lib.lib(), q, k, v, softmax_scale=softmax_scale, out=out,
+                        return_lse=return_lse)
+
+
+def forward_with(handle, q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, *,
+                 softmax_scale: float | None = None, out: torch.Tensor | None = None,
+                 return_lse: bool = False, split_kv: bool = True):
+    """attention_forward through one library build: `handle` is the product library or a
+    trace/ablation variant loaded with _lib.load. split_kv=False passes no workspace, so
+    every 512-row query block runs on one SM pair (the classic schedule)."""
     device = q.device
     for t, nm in ((q, "Q"), (k, "K"), (v, "V")):
         _check(t, nm, device)
@@ -74,21 +84,21 @@ def attention_forward(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, *,
             raise RuntimeError(f"out shape {tuple(out.shape)} must equal Q shape {tuple(q.shape)}")
     o4 = _as_bshd(out, "out")
     scale = (1.0 / math.sqrt(HEAD_DIM)) if softmax_scale is None else float(softmax_scale)
-    L = _lib.lib()
     with torch.cuda.device(device):
         # scratch for split KV ranges, from the caching allocator on this stream
-        ws_bytes = workspace_size(device)
-        ws = torch.empty(ws_bytes, dtype=torch.uint8, device=device)
+        ws_bytes = workspace_size(device) if split_kv else 0
+        ws = torch.empty(ws_bytes, dtype=torch.uint8, device=device) if split_kv else None
         stream = torch.cuda.current_stream(device).cuda_stream
         lse = torch.empty(B, H, Sq, dtype=torch.float32, device=device) if return_lse else None
-        rc = L.llmfa_forward_lse(
+        rc = handle.llmfa_forward_lse(
             ctypes.c_void_p(q4.data_ptr()), _lib.strides3(q4.stride()[:3]),
             ctypes.c_void_p(k4.data_ptr()), _lib.strides3(k4.stride()[:3]),
             ctypes.c_void_p(v4.data_ptr()), _lib.strides3(v4.stride()[:3]),
             ctypes.c_void_p(o4.data_ptr()), _lib.strides3(o4.stride()[:3]),
             ctypes.c_void_p(lse.data_ptr() if return_lse else None),
             _lib.strides2((H * Sq, Sq)),
-            B, H, Sq, Sk, ctypes.c_float(scale), ctypes.c_void_p(ws.data_ptr()), ws_bytes,
+            B, H, Sq, Sk, ctypes.c_float(scale),
+            ctypes.c_void_p(ws.data_ptr() if ws is not None else None), ws_bytes,
             ctypes.c_void_p(stream))
     _lib.check(rc, "llmfa_forward_lse")
     if return_lse:
@@ -147,6 +157,12 @@ def launch_plan(batch: int, heads: int, seq_q: int, seq_k: int,
                                             ctypes.byref(k), ctypes.byref(c), ctypes.byref(s)),
                "llmfa_launch_plan")
     return {"kernels": k.value, "clusters": c.value, "split_units": s.value}
+
+
+def build_info() -> dict:
+    """Compile-time configuration of the loaded library: ablation rung (0 = the product)
+    and whether the event trace is compiled in."""
+    return _lib.build_config()
 
 
 def max_active_clusters() -> int:

@@ -4,7 +4,13 @@ One nvcc invocation, no torch dependency in the binary (static cudart); the
 driver entry point for tensor-map encoding is resolved at run time, so the
 library builds on a machine without a GPU and loads on a machine with one.
 
-    python -m llm_fa_b200.build [--force] [-v]
+    python -m llm_fa_b200.build [--force] [-v] [--variant trace|floor|faux|noexp|all]
+
+Besides the product library, the same source builds variants (compile-time
+switches, each in its own library file, never loaded in place of the product):
+`trace` (-DLLMFA_TRACE=1: event trace and per-wait-site statistics) and the
+ablation-ladder rungs `floor`, `faux`, `noexp` (-DLLMFA_ABLATE=1..3: the TMA +
+MMA floor, no softmax math, no exponentials; their output is not attention).
 """
 from __future__ import annotations
 
@@ -37,19 +43,43 @@ def nvcc_path() -> str:
     raise RuntimeError("nvcc not found (set NVCC or put the CUDA toolkit on PATH)")
 
 
-def is_stale() -> bool:
-    if not LIB.exists():
+# variant name -> extra nvcc defines
+VARIANTS = {
+    "trace": ["-DLLMFA_TRACE=1"],
+    "floor": ["-DLLMFA_ABLATE=1"],
+    "faux": ["-DLLMFA_ABLATE=2"],
+    "noexp": ["-DLLMFA_ABLATE=3"],
+}
+
+
+def variant_path(name: str) -> Path:
+    return PKG / f"libllm_fa_b200_{name}.so"
+
+
+def is_stale(lib: Path = LIB) -> bool:
+    if not lib.exists():
         return True
-    t = LIB.stat().st_mtime
+    t = lib.stat().st_mtime
     return any(d.stat().st_mtime > t for d in DEPS)
 
 
 def build(force: bool = False, verbose: bool = False) -> Path:
-    """Compile the library if it is missing or older than its sources."""
-    if not force and not is_stale():
-        return LIB
-    tmp = LIB.with_suffix(".so.tmp")
-    cmd = [nvcc_path(), *NVCC_FLAGS, "-o", str(tmp), *map(str, SOURCES)]
+    """Compile the product library if it is missing or older than its sources."""
+    return _compile(LIB, [], force, verbose)
+
+
+def build_variant(name: str, force: bool = False, verbose: bool = False) -> Path:
+    """Compile one variant library (see VARIANTS) if missing or stale."""
+    if name not in VARIANTS:
+        raise ValueError(f"unknown variant {name!r}; one of {sorted(VARIANTS)}")
+    return _compile(variant_path(name), VARIANTS[name], force, verbose)
+
+
+def _compile(lib: Path, defines: list[str], force: bool, verbose: bool) -> Path:
+    if not force and not is_stale(lib):
+        return lib
+    tmp = lib.with_suffix(".so.tmp")
+    cmd = [nvcc_path(), *NVCC_FLAGS, *defines, "-o", str(tmp), *map(str, SOURCES)]
     proc = subprocess.run(cmd, capture_output=True, text=True)
     if verbose or proc.returncode != 0:
         sys.stderr.write(proc.stdout + proc.stderr)
@@ -59,13 +89,18 @@ def build(force: bool = False, verbose: bool = False) -> Path:
     for line in (proc.stdout + proc.stderr).splitlines():
         if "spill stores" in line and not line.strip().startswith("0 bytes stack frame, 0 bytes spill"):
             sys.stderr.write(f"warning: register spills reported by ptxas: {line.strip()}\n")
-    os.replace(tmp, LIB)
-    return LIB
+    os.replace(tmp, lib)
+    return lib
 
 
 if __name__ == "__main__":
     ap = argparse.ArgumentParser()
     ap.add_argument("--force", action="store_true")
     ap.add_argument("-v", "--verbose", action="store_true")
+    ap.add_argument("--variant", choices=[*VARIANTS, "all"])
     a = ap.parse_args()
-    print(build(force=a.force, verbose=a.verbose))
+    if a.variant is None:
+        print(build(force=a.force, verbose=a.verbose))
+    else:
+        for name in (VARIANTS if a.variant == "all" else [a.variant]):
+            print(build_variant(name, force=a.force, verbose=a.verbose))

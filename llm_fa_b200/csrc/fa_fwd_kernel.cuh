@@ -124,6 +124,24 @@ constexpr float kRescaleThreshold = 8.0f;  // log2 units
 #endif
 constexpr uint32_t kSoftmaxPolyMask = LLMFA_SOFTMAX_POLY_MASK;
 
+// Ablation ladder (compile-time; 0 in the product build). Each rung removes one
+// phase of the softmax so that its cost can be read off as a time difference,
+// as the reference's ladder kernels do (scaffolding.cu with SKIP_SM_FULL: the
+// TMA + MMA floor; faux.cu: no softmax math). The output of every rung other
+// than 0 is not attention; llmfa_build_config reports the rung, and the bench
+// refuses to time such a library as the product.
+//   1 floor     softmax and correction warps only take part in the barrier
+//               hand-offs (no TMEM loads or stores): TMA + MMA + epilogue
+//   2 faux      P = bf16(S): scores loaded and stored back, no row max, no
+//               scale, no exponentials, no row sums, no O rescale
+//   3 noexp     the full softmax (row max, rescale, row sums) with exp2(x)
+//               replaced by x: what the exponentials cost
+#ifndef LLMFA_ABLATE
+#define LLMFA_ABLATE 0
+#endif
+constexpr int kAblate = LLMFA_ABLATE;
+static_assert(kAblate >= 0 && kAblate <= 3, "LLMFA_ABLATE must be 0..3");
+
 // Device status word: 0 = ok; otherwise kStatusTimeoutBase + wait-site id.
 constexpr int kStatusTimeoutBase = 0x1000;
 enum WaitSite : int {
@@ -272,8 +290,30 @@ __device__ __forceinline__ bool mbar_wait_slow(uint32_t bar, uint32_t parity, co
     }
   }
 }
+#if LLMFA_TRACE
+// Per-wait-site statistics of the attention kernel (trace builds only): lane 0
+// of every waiting warp adds the %clock64 cycles it spent in the wait and a
+// count to this CTA's slot of the site; the CTA's totals go to g_wait_stats at
+// teardown. Slot 0 holds the CTAs' own run time (cycles, CTA count).
+constexpr int kWaitSlots = 16;
+__device__ unsigned long long g_wait_stats[kWaitSlots * 2];
+__shared__ unsigned long long g_wait_acc[kWaitSlots * 2];
+#endif
+
 __device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, const WaitCtl& c,
                                           int site, bool honor_abort = true) {
+#if LLMFA_TRACE
+  if (site <= kSiteDrain) {  // the attention kernel's sites (its prologue clears the slots)
+    const long long t0 = clock64();
+    const bool ok = ptx::mbar_try_wait(bar, parity) ||
+                    mbar_wait_slow(bar, parity, c, site, honor_abort);
+    if ((threadIdx.x & 31u) == 0) {
+      atomicAdd(&g_wait_acc[2 * site], static_cast<unsigned long long>(clock64() - t0));
+      atomicAdd(&g_wait_acc[2 * site + 1], 1ull);
+    }
+    return ok;
+  }
+#endif
   if (ptx::mbar_try_wait(bar, parity)) return true;
   return mbar_wait_slow(bar, parity, c, site, honor_abort);
 }
@@ -473,15 +513,22 @@ __device__ __forceinline__ void mask_tail(uint32_t (&r)[32], int col0, int kv_ta
 }
 
 // 32 scores -> 16 bf16x2 probabilities stored to TMEM at `t_p`; adds the fp32
-// probabilities to the running pair sum.
+// probabilities to the running pair sum. (Ablation rungs: faux stores bf16(s)
+// and sums nothing; noexp stores and sums x = s * scale*log2e - m.)
 __device__ __forceinline__ void exp_chunk(const uint32_t (&r)[32], uint64_t c2, uint64_t neg_m2,
                                           uint64_t& lsum2, uint32_t t_p) {
   uint32_t pk[16];
 #pragma unroll
   for (int k = 0; k < 16; ++k) {
+    if constexpr (kAblate == 2) {
+      pk[k] = ptx::bf16x2_pack(__uint_as_float(r[2 * k]), __uint_as_float(r[2 * k + 1]));
+      continue;
+    }
     const uint64_t x2 = ptx::f2_fma(
         ptx::f2_pack(__uint_as_float(r[2 * k]), __uint_as_float(r[2 * k + 1])), c2, neg_m2);
-    const uint64_t e2 = ((kSoftmaxPolyMask >> k) & 1u) ? exp2_poly_x2(x2) : exp2_mufu_x2(x2);
+    uint64_t e2;
+    if constexpr (kAblate == 3) e2 = x2;
+    else e2 = ((kSoftmaxPolyMask >> k) & 1u) ? exp2_poly_x2(x2) : exp2_mufu_x2(x2);
     lsum2 = ptx::f2_add(lsum2, e2);
     float e0, e1;
     ptx::f2_unpack(e2, e0, e1);
@@ -544,6 +591,10 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
     g_cta_abort = 0u;
     ptx::fence_mbar_init();
   }
+#if LLMFA_TRACE
+  const long long cta_t0 = clock64();
+  if (threadIdx.x < 2 * kWaitSlots) g_wait_acc[threadIdx.x] = 0ull;
+#endif
   if (warp == 12) {
     ptx::tmem_alloc<2>(smem_base + kSmemTmemSlot, 512);
     ptx::tmem_relinquish<2>();
@@ -590,6 +641,14 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
         }
         s_phase ^= 1u;
         if (quarter == 0 && lane == 0) LLMFA_TRACE_EVENT(kEvSReady, tile, j);
+        if constexpr (kAblate == 1) {  // floor: the hand-offs only
+          if (lane == 0) {
+            ptx::mbar_arrive(stat_bar);
+            ptx::mbar_arrive_cluster(phalf_leader);
+            ptx::mbar_arrive_cluster(pfull_leader);
+          }
+          continue;
+        }
         ptx::tc_fence_after();
         // Pass 1: all 128 scores -> row max. Chunks 0-1 stay in registers;
         // chunks 2-3 (columns 64-127, never overwritten by P) are re-read from
@@ -615,8 +674,11 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
             mask_tail(s2, 64, p.kv_tail);
             mask_tail(s3, 96, p.kv_tail);
           }
-          mt = fmaxf(fmaxf(chunk_max(s0), chunk_max(s1)), fmaxf(chunk_max(s2), chunk_max(s3))) *
-               p.scale_log2;
+          if constexpr (kAblate == 2)  // faux: no row max
+            mt = 0.f;
+          else
+            mt = fmaxf(fmaxf(chunk_max(s0), chunk_max(s1)), fmaxf(chunk_max(s2), chunk_max(s3))) *
+                 p.scale_log2;
         }
         float sc = 1.f;
         if (j == 0) {
@@ -714,6 +776,13 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
           }
           stat_phase ^= 1u << tile;
           if (warp == 8 && lane == 0) LLMFA_TRACE_EVENT(kEvCorrStat, tile, j);
+          if constexpr (kAblate == 1) {  // floor: the hand-offs only
+            if (lane == 0) {
+              if (j > 0) ptx::mbar_arrive_cluster(ptx::mapa(bar(kBarPHalf + tile), 0));
+              ptx::mbar_arrive_cluster(ptx::mapa(bar(kBarPFull + tile), 0));
+            }
+            continue;
+          }
           const float sc = sm_scale[tile * kBlockM + row];
           const float mcur = sm_mcur[tile * kBlockM + row];
           if (j > 0 && __any_sync(0xffffffffu, sc != 1.f)) {
@@ -795,7 +864,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
         // for a piece of a unit split across clusters (llm_fa_combine_kernel
         // merges the pieces).
         const float lsum = sm_lsum[(sp * kQTiles + tile) * kBlockM + row] + (tile == 0 ? lc0 : lc1);
-        const float inv_l = __frcp_rn(lsum);
+        // (floor and faux rungs keep no row sum: no final division, as faux.cu)
+        const float inv_l = (kAblate == 1 || kAblate == 2) ? 1.f : __frcp_rn(lsum);
         const int row_blk = tile * (kBlockM * kPair) + static_cast<int>(rank) * kBlockM;
         if (kWithLse && sg.slot < 0 && uc.row0 + row_blk + row < p.Sq) {
           // sum_k exp(s_k * scale) = 2^m * l with m in log2 units
@@ -1144,6 +1214,14 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
   asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
   ptx::tc_fence_before();
   __syncthreads();
+#if LLMFA_TRACE
+  if (threadIdx.x == 0) {
+    g_wait_acc[0] = static_cast<unsigned long long>(clock64() - cta_t0);
+    g_wait_acc[1] = 1ull;
+  }
+  __syncthreads();
+  if (threadIdx.x < 2 * kWaitSlots) atomicAdd(&g_wait_stats[threadIdx.x], g_wait_acc[threadIdx.x]);
+#endif
   ptx::cluster_sync();
   if (warp == 12) {
     ptx::tc_fence_after();

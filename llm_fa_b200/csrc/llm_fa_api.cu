@@ -200,6 +200,13 @@ extern "C" {
 
 int llmfa_version(void) { return kVersion; }
 
+int llmfa_build_config(int* ablation, int* trace) {
+  if (ablation == nullptr || trace == nullptr) return LLMFA_ERR_INVALID_ARGUMENT;
+  *ablation = llmfa::kAblate;
+  *trace = LLMFA_TRACE;
+  return LLMFA_OK;
+}
+
 const char* llmfa_error_string(int status) {
   switch (status) {
     case LLMFA_OK: return "ok";
@@ -239,21 +246,23 @@ int llmfa_forward(const void* q, const int64_t q_strides[3], const void* k,
                            workspace_bytes, stream);
 }
 
-int llmfa_forward_lse(const void* q, const int64_t q_strides[3], const void* k,
-                      const int64_t k_strides[3], const void* v, const int64_t v_strides[3],
-                      void* o, const int64_t o_strides[3], float* lse,
-                      const int64_t lse_strides[2], int64_t batch, int64_t heads, int64_t seq_q,
-                      int64_t seq_k, float softmax_scale, void* workspace,
-                      uint64_t workspace_bytes, void* stream) {
-  // ---- argument checks (no CUDA call before they pass)
+}  // extern "C"
+
+namespace {
+
+// Argument checks shared by every compute entry point; makes no CUDA call.
+int check_forward_args(const void* q, const int64_t q_strides[3], const void* k,
+                       const int64_t k_strides[3], const void* v, const int64_t v_strides[3],
+                       const void* o, const int64_t o_strides[3], const float* lse,
+                       const int64_t lse_strides[2], int64_t batch, int64_t heads, int64_t seq_q,
+                       int64_t seq_k, float softmax_scale) {
   if (batch < 1 || heads < 1 || seq_q < 1 || seq_k < 1) return LLMFA_ERR_INVALID_ARGUMENT;
   if (!(softmax_scale > 0.f) || !std::isfinite(softmax_scale)) return LLMFA_ERR_INVALID_ARGUMENT;
   if (seq_q >= (int64_t(1) << 31) || seq_k >= (int64_t(1) << 31) || heads >= (1 << 24) ||
       batch >= (1 << 24))
     return LLMFA_ERR_UNSUPPORTED;
   const int64_t n_qblk = (seq_q + llmfa::kUnitRows - 1) / llmfa::kUnitRows;
-  const int64_t n_units = batch * heads * n_qblk;
-  if (n_units >= (int64_t(1) << 31)) return LLMFA_ERR_UNSUPPORTED;
+  if (batch * heads * n_qblk >= (int64_t(1) << 31)) return LLMFA_ERR_UNSUPPORTED;
   int rc;
   if ((rc = check_view(q, q_strides, seq_q, heads, batch)) != LLMFA_OK) return rc;
   if ((rc = check_view(k, k_strides, seq_k, heads, batch)) != LLMFA_OK) return rc;
@@ -265,6 +274,25 @@ int llmfa_forward_lse(const void* q, const int64_t q_strides[3], const void* k,
     if ((batch > 1 && lse_strides[0] < 1) || (heads > 1 && lse_strides[1] < 1))
       return LLMFA_ERR_INVALID_ARGUMENT;
   }
+  return LLMFA_OK;
+}
+
+}  // namespace
+
+extern "C" {
+
+int llmfa_forward_lse(const void* q, const int64_t q_strides[3], const void* k,
+                      const int64_t k_strides[3], const void* v, const int64_t v_strides[3],
+                      void* o, const int64_t o_strides[3], float* lse,
+                      const int64_t lse_strides[2], int64_t batch, int64_t heads, int64_t seq_q,
+                      int64_t seq_k, float softmax_scale, void* workspace,
+                      uint64_t workspace_bytes, void* stream) {
+  // ---- argument checks (no CUDA call before they pass)
+  int rc = check_forward_args(q, q_strides, k, k_strides, v, v_strides, o, o_strides, lse,
+                              lse_strides, batch, heads, seq_q, seq_k, softmax_scale);
+  if (rc != LLMFA_OK) return rc;
+  const int64_t n_qblk = (seq_q + llmfa::kUnitRows - 1) / llmfa::kUnitRows;
+  const int64_t n_units = batch * heads * n_qblk;
 
   int dev = 0;
   DeviceSetup* s = nullptr;
@@ -451,6 +479,17 @@ int llmfa_trace_read(void* dst_host, uint64_t capacity_bytes, uint64_t* written_
       return LLMFA_ERR_CUDA;
     }
     *written_bytes = bytes + seg_bytes;
+    const uint64_t wait_bytes = sizeof(llmfa::g_wait_stats);
+    if (capacity_bytes >= bytes + seg_bytes + wait_bytes) {  // then the wait-site statistics
+      static const unsigned long long zeros[2 * llmfa::kWaitSlots] = {};
+      if (cudaMemcpyFromSymbol(static_cast<char*>(dst_host) + bytes + seg_bytes,
+                               llmfa::g_wait_stats, wait_bytes) != cudaSuccess ||
+          cudaMemcpyToSymbol(llmfa::g_wait_stats, zeros, wait_bytes) != cudaSuccess) {
+        cudaGetLastError();
+        return LLMFA_ERR_CUDA;
+      }
+      *written_bytes = bytes + seg_bytes + wait_bytes;
+    }
   }
   return LLMFA_OK;
 #else
@@ -502,6 +541,12 @@ extern "C" int llmfa_forward_static_scratch(const void* q, const int64_t q_strid
                                             const int64_t o_strides[3], int64_t batch,
                                             int64_t heads, int64_t seq_q, int64_t seq_k,
                                             float softmax_scale, void* stream) {
+  // The same checks as llmfa_forward, before any CUDA call (the symbol lookup
+  // below loads the module and its 20 MB array).
+  const int arg_rc = check_forward_args(q, q_strides, k, k_strides, v, v_strides, o, o_strides,
+                                        nullptr, nullptr, batch, heads, seq_q, seq_k,
+                                        softmax_scale);
+  if (arg_rc != LLMFA_OK) return arg_rc;
   int dev = 0;
   if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices) {
     cudaGetLastError();

@@ -29,35 +29,134 @@ TRACE_ITERS = 16
 RECORD = np.dtype([("globaltimer_ns", "<u8"), ("clock", "<i8")])
 
 
-def read_trace() -> np.ndarray:
-    """Structured array [cta rank 2][Q tile 2][event][iteration] of (globaltimer_ns, clock)."""
-    n = 2 * 2 * len(EVENTS) * TRACE_ITERS
-    buf = np.zeros(n, dtype=RECORD)
-    written = ctypes.c_uint64(0)
-    rc = _lib.lib().llmfa_trace_read(ctypes.c_void_p(buf.ctypes.data), buf.nbytes,
-                                     ctypes.byref(written))
-    _lib.check(rc, "llmfa_trace_read (library built without LLMFA_TRACE=1?)")
-    return buf.reshape(2, 2, len(EVENTS), TRACE_ITERS)
-
-
 SEG_CLUSTERS = 160
 SEG_SEGMENTS = 32
+WAIT_SLOTS = 16
+# Bounded-wait sites of the attention kernel (WaitSite in fa_fwd_kernel.cuh): id -> (role,
+# what the waiting warp waits for). Slot 0 of the statistics holds the CTAs' run time.
+WAIT_SITES = {
+    1: ("producer", "Q tile slot free (last QK of the previous unit done)"),
+    2: ("producer", "K/V stage free (MMAs that read it done)"),
+    3: ("mma", "Q tile landed"),
+    4: ("mma", "K/V stage landed"),
+    5: ("mma", "P published (half or full) by softmax + correction warps"),
+    6: ("softmax", "S = QK^T in TMEM"),
+    7: ("correction", "rescale factor published by the softmax warp"),
+    8: ("correction", "end-of-segment row sum published"),
+    9: ("correction", "O complete in TMEM (last PV of the segment)"),
+    10: ("correction", "O staging buffer free / filled (TMA store)"),
+    11: ("mma", "teardown drain of the last MMAs"),
+}
+# warps of one CTA that wait at each role's sites (lane 0 of each is counted)
+ROLE_WARPS = {"producer": 1, "mma": 1, "softmax": 8, "correction": 4}
+
+_EV_BYTES = 2 * 2 * len(EVENTS) * TRACE_ITERS * RECORD.itemsize
+_SEG_BYTES = SEG_CLUSTERS * SEG_SEGMENTS * 4 * 8
+_WAIT_BYTES = WAIT_SLOTS * 2 * 8
 
 
-def read_segments() -> np.ndarray:
-    """Segment timeline of every cluster, uint64 [cluster][segment][4]:
-    %globaltimer of the first QK, of the epilogue seeing O complete, of the
-    epilogue done, then u * 65536 + len (all zero for segments not run)."""
-    n_ev = 2 * 2 * len(EVENTS) * TRACE_ITERS * RECORD.itemsize
-    n_seg = SEG_CLUSTERS * SEG_SEGMENTS * 4 * 8
-    buf = np.zeros(n_ev + n_seg, dtype=np.uint8)
+def _read(handle, nbytes: int) -> tuple[np.ndarray, int]:
+    h = _lib.lib() if handle is None else handle
+    buf = np.zeros(nbytes, dtype=np.uint8)
     written = ctypes.c_uint64(0)
-    rc = _lib.lib().llmfa_trace_read(ctypes.c_void_p(buf.ctypes.data), buf.nbytes,
-                                     ctypes.byref(written))
+    rc = h.llmfa_trace_read(ctypes.c_void_p(buf.ctypes.data), buf.nbytes, ctypes.byref(written))
     _lib.check(rc, "llmfa_trace_read (library built without LLMFA_TRACE=1?)")
-    if written.value < n_ev + n_seg:
-        raise RuntimeError("library trace has no segment timeline")
-    return buf[n_ev:].view(np.uint64).reshape(SEG_CLUSTERS, SEG_SEGMENTS, 4)
+    return buf, written.value
+
+
+def read_trace(handle=None) -> np.ndarray:
+    """Structured array [cta rank 2][Q tile 2][event][iteration] of (globaltimer_ns, clock).
+    `handle`: a library loaded with _lib.load (default: the product library)."""
+    buf, _ = _read(handle, _EV_BYTES)
+    return buf.view(RECORD).reshape(2, 2, len(EVENTS), TRACE_ITERS)
+
+
+def read_all(handle=None) -> tuple[np.ndarray, np.ndarray, np.ndarray]:
+    """(events, segment timeline, wait statistics) in one read; the read clears the wait
+    statistics. Segment timeline: uint64 [cluster][segment][4] = %globaltimer of the first
+    QK, of the epilogue seeing O complete, of the epilogue done, then u * 65536 + len
+    (zero for segments not run). Wait statistics: uint64 [16][2] (see WAIT_SITES)."""
+    buf, written = _read(handle, _EV_BYTES + _SEG_BYTES + _WAIT_BYTES)
+    if written < _EV_BYTES + _SEG_BYTES + _WAIT_BYTES:
+        raise RuntimeError("library trace has no segment timeline / wait statistics")
+    ev = buf[:_EV_BYTES].view(RECORD).reshape(2, 2, len(EVENTS), TRACE_ITERS)
+    seg = buf[_EV_BYTES:_EV_BYTES + _SEG_BYTES].view(np.uint64).reshape(
+        SEG_CLUSTERS, SEG_SEGMENTS, 4)
+    wait = buf[_EV_BYTES + _SEG_BYTES:].view(np.uint64).reshape(WAIT_SLOTS, 2)
+    return ev, seg, wait
+
+
+def read_segments(handle=None) -> np.ndarray:
+    """Segment timeline of every cluster (see read_all)."""
+    return read_all(handle)[1]
+
+
+def wait_table(wait: np.ndarray, clock_ghz: float) -> list[dict]:
+    """Per wait site: waits per CTA, mean wait, and the share of the waiting warps' time
+    spent there (cycles waited / (warps of the role x CTA run cycles))."""
+    cta_cycles, ctas = float(wait[0, 0]), max(float(wait[0, 1]), 1.0)
+    rows = []
+    for site, (role, what) in WAIT_SITES.items():
+        cyc, n = float(wait[site, 0]), float(wait[site, 1])
+        if n == 0:
+            continue
+        rows.append({"site": site, "role": role, "waits_for": what,
+                     "waits_per_cta": n / ctas,
+                     "mean_wait_ns": cyc / n / clock_ghz,
+                     "share_of_role_time": cyc / (ROLE_WARPS[role] * cta_cycles)})
+    return rows
+
+
+# The hand-off chain of one Q tile's KV iteration j, as causal edges (a, b, b's iteration
+# offset): the softmax warps' program order, each barrier hand-off to the leader's MMA warp
+# and the MMA warp's program order, and QK(j+1) -> S(j+1) visible.
+CHAIN_EDGES = [
+    ("s_ready", "ld_done", 0), ("ld_done", "stat", 0), ("stat", "p_half", 0),
+    ("p_half", "p_full", 0),
+    ("p_half", "mma_p_half", 0), ("p_full", "mma_p_full", 0),
+    ("mma_p_half", "mma_p_full", 0), ("mma_p_full", "mma_qk_next", 0),
+    ("mma_qk_next", "s_ready", 1),
+]
+CHAIN_EVENTS = ["s_ready", "ld_done", "stat", "p_half", "p_full", "mma_p_half", "mma_p_full",
+                "mma_qk_next"]
+
+
+def check_chain(tr: np.ndarray, slack_ns: float = 64.0) -> list[str]:
+    """Walk every traced iteration's hand-off chain (CHAIN_EDGES) for both Q tiles and both
+    CTAs; return the violations (empty = every event present and every edge in order).
+    Within one SM (the leader CTA's softmax and MMA warps) the order is checked on
+    %clock64; the peer CTA's softmax events against the leader's MMA events on
+    %globaltimer, whose resolution is 32 ns, with `slack_ns` of tolerance. Edges into the
+    next iteration are checked for all but the window's last iteration."""
+    E = {e: i for i, e in enumerate(EVENTS)}
+    bad = []
+    for r in (0, 1):
+        for t in (0, 1):
+            for name in CHAIN_EVENTS:
+                src = 0 if ROLES[name] == "mma" else r
+                missing = np.nonzero(tr[src, t, E[name]]["globaltimer_ns"] == 0)[0]
+                if len(missing):
+                    bad.append(f"cta{r} tile{t}: {name} missing at iterations "
+                               f"{[TRACE_FIRST + int(i) for i in missing]}")
+            for i in range(TRACE_ITERS):
+                for a, b, off in CHAIN_EDGES:
+                    j_b = i + off
+                    if j_b >= TRACE_ITERS:
+                        continue
+                    ra = 0 if ROLES[a] == "mma" else r
+                    rb = 0 if ROLES[b] == "mma" else r
+                    if ra == rb:  # same SM: cycle counter
+                        ta = int(tr[ra, t, E[a]]["clock"][i])
+                        tb = int(tr[rb, t, E[b]]["clock"][j_b])
+                        ok = tb >= ta
+                    else:
+                        ta = float(tr[ra, t, E[a]]["globaltimer_ns"][i])
+                        tb = float(tr[rb, t, E[b]]["globaltimer_ns"][j_b])
+                        ok = tb + slack_ns >= ta
+                    if not ok:
+                        bad.append(f"cta{r} tile{t} iteration {TRACE_FIRST + i}: {a} -> {b} "
+                                   f"out of order ({ta} > {tb})")
+    return bad
 
 
 def clock_ghz(tr: np.ndarray) -> float:
@@ -149,3 +248,61 @@ def to_chrome_json(tr: np.ndarray, path: str, clock_ghz: float) -> None:
                                    "args": {"iteration": TRACE_FIRST + i}})
     with open(path, "w") as f:
         json.dump({"traceEvents": events, "displayTimeUnit": "ns"}, f)
+
+
+def main() -> None:
+    """python -m llm_fa_b200.trace [--config c3] [--chrome out.json]: build the trace
+    variant, run the configuration through it, and print the per-hop latencies, the
+    hand-off chain check and the per-wait-site table (markdown)."""
+    import argparse
+
+    import torch
+
+    from .attention import forward_with
+    from .build import build_variant
+    from .workloads import CONFIGS, make_inputs
+
+    ap = argparse.ArgumentParser(description=main.__doc__.splitlines()[0])
+    ap.add_argument("--config", default="c3")
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--chrome", default=None, help="write a Chrome trace-event JSON here")
+    a = ap.parse_args()
+    h = _lib.load(build_variant("trace"))
+    if not _lib.build_config(h)["trace"]:
+        raise RuntimeError("trace variant built without LLMFA_TRACE")
+    cfg = CONFIGS[a.config]
+    dev = torch.device("cuda", 0)
+    q, k, v = (t.to(dev) for t in make_inputs(cfg))
+    o = torch.empty_like(q)
+    for _ in range(a.warmup):
+        forward_with(h, q, k, v, out=o)
+    torch.cuda.synchronize()
+    read_all(h)  # clears the wait statistics of the warm-up launches
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    forward_with(h, q, k, v, out=o)
+    e1.record()
+    torch.cuda.synchronize()
+    ev, seg, wait = read_all(h)
+    ghz = clock_ghz(ev)
+    print(f"# trace build, {cfg.name} ({cfg.describe()}): {e0.elapsed_time(e1):.3f} ms, "
+          f"SM clock {ghz:.3f} GHz (from the trace)")
+    print("\n## hand-off latencies (median over the traced window, ns)\n")
+    for name, val in hop_latencies(ev, ghz).items():
+        print(f"- {name}: {val:.0f}")
+    bad = check_chain(ev)
+    print(f"\n## chain check: {'ok' if not bad else f'{len(bad)} violations'}")
+    for b in bad[:20]:
+        print(f"- {b}")
+    print("\n## wait sites (all CTAs of the launch)\n")
+    print("| site | role | waits for | waits per CTA | mean wait (ns) | share of the role's time |")
+    print("|---|---|---|---|---|---|")
+    for r in wait_table(wait, ghz):
+        print(f"| {r['site']} | {r['role']} | {r['waits_for']} | {r['waits_per_cta']:.1f} | "
+              f"{r['mean_wait_ns']:.0f} | {100 * r['share_of_role_time']:.1f} % |")
+    if a.chrome:
+        to_chrome_json(ev, a.chrome, ghz)
+
+
+if __name__ == "__main__":
+    main()

@@ -44,7 +44,9 @@ def input_checksum(q, k, v) -> np.ndarray:
 
 
 def main() -> None:
-    ref_dir = Path(sys.argv[1] if len(sys.argv) > 1 else "/root/reference")
+    if len(sys.argv) < 2:
+        sys.exit("usage: python tests/golden/make_golden.py <reference checkout>")
+    ref_dir = Path(sys.argv[1])
     torch_sdpa = load_reference_sdpa(ref_dir)
     out = {}
     for name, (cfg, nrows) in CASES.items():

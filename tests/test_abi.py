@@ -88,6 +88,23 @@ def test_lse_entry_point_rejects_bad_lse_arguments_without_cuda(L):
                                None) == _lib.LLMFA_ERR_INVALID_ARGUMENT
 
 
+def test_static_scratch_entry_point_checks_arguments_without_cuda(L):
+    """llmfa_forward_static_scratch refuses invalid arguments with llmfa_forward's status
+    codes before its first CUDA call (the device-address lookup of its fixed array)."""
+    st = _lib.strides3((1024 * 128, 128, 128))
+    p = ctypes.c_void_p(16)
+    scale = ctypes.c_float(0.088)
+
+    def call(q=p, k=p, Sq=1024, sc=scale):
+        return L.llmfa_forward_static_scratch(q, st, k, st, p, st, p, st, 1, 1, Sq, 1024, sc,
+                                              None)
+
+    assert call(q=None) == _lib.LLMFA_ERR_INVALID_ARGUMENT
+    assert call(sc=ctypes.c_float(0.0)) == _lib.LLMFA_ERR_INVALID_ARGUMENT
+    assert call(Sq=0) == _lib.LLMFA_ERR_INVALID_ARGUMENT
+    assert call(k=ctypes.c_void_p(24)) == _lib.LLMFA_ERR_UNSUPPORTED  # not 16-byte aligned
+
+
 def test_small_helpers_validate(L):
     assert L.llmfa_set_wait_timeout_ms(0) == _lib.LLMFA_ERR_INVALID_ARGUMENT
     assert L.llmfa_device_status(None, None) == _lib.LLMFA_ERR_INVALID_ARGUMENT
@@ -103,3 +120,36 @@ def test_python_wrapper_rejects_cpu_tensors():
     x = torch.zeros(512, 128, dtype=torch.bfloat16)
     with pytest.raises(RuntimeError, match="CUDA"):
         attention_forward(x, x, x)
+
+
+def test_product_build_has_no_ablation_or_trace(L):
+    """The default library is the product: no ablation-ladder rung, no event trace."""
+    cfg = _lib.build_config(L)
+    assert cfg == {"ablation": 0, "ablation_name": "none", "trace": False}
+    a, t = ctypes.c_int(-1), ctypes.c_int(-1)
+    assert L.llmfa_build_config(None, ctypes.byref(t)) == _lib.LLMFA_ERR_INVALID_ARGUMENT
+    assert L.llmfa_build_config(ctypes.byref(a), ctypes.byref(t)) == _lib.LLMFA_OK
+
+
+def test_ablation_variant_reports_its_rung():
+    """A ladder rung is a separate library file that says what it is (no GPU needed)."""
+    from llm_fa_b200.build import build_variant
+    h = _lib.load(build_variant("floor"))
+    assert _lib.build_config(h) == {"ablation": 1, "ablation_name": "floor", "trace": False}
+
+
+def test_bench_refuses_an_ablation_build(monkeypatch):
+    """bench.py times only the product: a library reporting an ablation rung is refused
+    before any GPU work."""
+    import argparse
+
+    import llm_fa_b200
+
+    import bench
+    from llm_fa_b200.workloads import CONFIGS
+    monkeypatch.setattr(llm_fa_b200, "build_info",
+                        lambda: {"ablation": 1, "ablation_name": "floor", "trace": False})
+    args = argparse.Namespace(warmup=3, steps=1, no_e2e=True, no_cpu_baseline=True,
+                              validate=False, cpu_seconds=1.0)
+    with pytest.raises(RuntimeError, match="ablation"):
+        bench.run_ours(args, CONFIGS["c1"], 1, 0, 0)

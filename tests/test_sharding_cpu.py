@@ -92,6 +92,27 @@ def test_head_sharding_covers_every_head_once():
     assert bench.local_shard(Config("one", 1, 1, 64, 64, 0), 2, 0) == ("replica",)
 
 
+def test_single_head_configs_shard_query_rows():
+    """One (batch, head): whole 512-row query blocks per rank, K and V on every rank; the
+    row shards of all ranks tile the query rows once."""
+    from llm_fa_b200.workloads import CONFIGS
+    c3 = CONFIGS["c3"]
+    for world in (2, 4, 8):
+        shards = [bench.local_shard(c3, world, r) for r in range(world)]
+        assert all(s[0] == "rows" and (s[2] - s[1]) % 512 == 0 for s in shards)
+        assert [s[1] for s in shards] == sorted(s[1] for s in shards)
+        assert shards[0][1] == 0 and shards[-1][2] == c3.seq_q
+        assert all(a[2] == b[1] for a, b in zip(shards, shards[1:]))
+    cfg = Config("rows", 1, 1, 2048, 320, seed=33)
+    q, k, v = make_inputs(cfg)
+    parts = []
+    for r in range(4):
+        ql, kl, vl = bench.slice_inputs(q, k, v, bench.local_shard(cfg, 4, r))
+        assert kl.shape == k.shape and vl.shape == v.shape
+        parts.append(sdpa_fp32(ql, kl, vl))
+    assert float((torch.cat(parts, dim=1) - sdpa_fp32(q, k, v)).abs().max()) < 1e-6
+
+
 def test_two_gloo_ranks_gather_the_whole_output():
     q = _spawn(_shard_and_gather)
     status, err = q.get(timeout=10)

@@ -44,3 +44,30 @@ def test_chrome_export(tmp_path):
     assert min(e["ts"] for e in events) >= 0.0
     rows = trace.timeline(tr, 1.8, rank=0, first=2, count=1)
     assert rows[0][0] == 0.0 and rows[0][1].endswith("tile0 s_ready")
+
+
+def test_chain_check_accepts_the_schedule_and_reports_a_reordering():
+    tr = _synthetic()
+    assert trace.check_chain(tr) == []
+    E = {e: i for i, e in enumerate(trace.EVENTS)}
+    bad = tr.copy()
+    # the leader's MMA warp "sees" tile 1's P half before CTA 0 published it
+    bad[0, 1, E["mma_p_half"], 3]["clock"] = bad[0, 1, E["p_half"], 3]["clock"] - 100
+    msgs = trace.check_chain(bad)
+    assert msgs and all("p_half -> mma_p_half" in m for m in msgs), msgs
+    gone = tr.copy()
+    gone[1, 0, E["stat"], 5]["globaltimer_ns"] = 0
+    assert any("stat missing" in m for m in trace.check_chain(gone))
+
+
+def test_wait_table_shares():
+    wait = np.zeros((trace.WAIT_SLOTS, 2), dtype=np.uint64)
+    wait[0] = (2 * 1_000_000, 2)      # two CTAs of 1e6 cycles
+    wait[6] = (8 * 2 * 250_000, 400)  # softmax S waits: 8 warps x 2 CTAs x 250k cycles
+    wait[4] = (2 * 100_000, 60)       # MMA K/V waits
+    rows = {r["site"]: r for r in trace.wait_table(wait, clock_ghz=2.0)}
+    assert set(rows) == {4, 6}
+    assert abs(rows[6]["share_of_role_time"] - 0.25) < 1e-12
+    assert abs(rows[4]["share_of_role_time"] - 0.10) < 1e-12
+    assert abs(rows[6]["waits_per_cta"] - 200.0) < 1e-12
+    assert abs(rows[6]["mean_wait_ns"] - 2 * 8 * 250_000 / 400 / 2.0) < 1e-9
