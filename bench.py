@@ -31,7 +31,6 @@ import argparse
 import json
 import os
 import statistics
-import subprocess
 import sys
 import time
 from datetime import timedelta
@@ -40,9 +39,11 @@ from pathlib import Path
 ROOT = Path(__file__).resolve().parent
 sys.path.insert(0, str(ROOT))
 
+from llm_fa_b200.gpuclocks import ClockSampler  # noqa: E402
+
 METRIC = "attn fwd TFLOP/s bf16 hd128 & % of tensor peak; µs vs llm_fa.cu/FA4 same box"
 UNIT = "TFLOP/s"
-DATA = "synthetic (seeded N(0,1) bf16 inputs at the BASELINE.json shapes, drawn on the CPU)"
+DATA = "synthetic (seeded N(0,1) bf16 inputs at the configuration's shapes, drawn on the CPU)"
 # The reference's published TFLOP/s for two of the configurations, computed from its
 # published kernel microseconds (llm_fa.cu at 16384^2 and 32768x131072), which were measured
 # under ncu with the SM clock locked near 1.07 GHz: not comparable with CUDA-event timings
@@ -64,7 +65,7 @@ def parse_args():
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=20)
     ap.add_argument("--warmup", type=int, default=5)
-    ap.add_argument("--config", default="c3", help="c1..c5 (BASELINE.json configs)")
+    ap.add_argument("--config", default="c3", help="c1..c5 (llm_fa_b200.workloads.CONFIGS)")
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
@@ -92,69 +93,6 @@ def measured_peaks() -> dict:
         except Exception:
             pass
     return {}
-
-
-class ClockSampler:
-    """nvidia-smi samples (200 ms) of one GPU while the timed region runs.
-
-    nvidia-smi writes its samples to a file (`-f`), read after the timed region: a
-    Python thread reading a pipe would take the interpreter lock during the timed
-    steps and delay their launches."""
-
-    FIELDS = ("clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
-              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
-              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
-
-    def __init__(self, index: int):
-        self.index = index
-        self.proc = None
-        self.lines: list[str] = []
-        self.path = None
-
-    def start(self):
-        import tempfile
-        fd, self.path = tempfile.mkstemp(prefix="llmfa_clocks_", suffix=".csv")
-        os.close(fd)
-        try:
-            self.proc = subprocess.Popen(
-                ["nvidia-smi", f"--id={self.index}", f"--query-gpu={self.FIELDS}",
-                 "--format=csv,noheader,nounits", "-lms", "200", "-f", self.path],
-                stdout=subprocess.DEVNULL, stderr=subprocess.DEVNULL)
-        except (OSError, ValueError):
-            self.proc = None
-
-    def stop(self) -> dict | None:
-        if self.proc is None:
-            return None
-        self.proc.terminate()
-        try:
-            self.proc.wait(timeout=5)
-        except subprocess.TimeoutExpired:
-            self.proc.kill()
-        try:
-            with open(self.path) as f:
-                self.lines = [ln.strip() for ln in f]
-            os.unlink(self.path)
-        except OSError:
-            self.lines = []
-        sm, mx, reasons = [], [], set()
-        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
-        for ln in self.lines:
-            parts = [x.strip() for x in ln.split(",")]
-            if len(parts) < 8:
-                continue
-            try:
-                sm.append(float(parts[0]))
-                mx.append(float(parts[1]))
-            except ValueError:
-                continue
-            for nm, val in zip(names, parts[4:8]):
-                if val.lower() == "active":
-                    reasons.add(nm)
-        if not sm:
-            return None
-        return {"sm_mhz": statistics.median(sm), "sm_max_mhz": max(mx), "reasons": sorted(reasons),
-                "samples": len(sm)}
 
 
 # ------------------------------------------------------------------ workload

@@ -125,7 +125,8 @@ int llmfa_version(void);
  * Compile-time configuration of this library build: `*ablation` = the
  * ablation-ladder rung (0 = the product; 1 = TMA + MMA floor, 2 = no softmax
  * math, 3 = no exponentials: the output of rungs 1-3 is not attention) and
- * `*trace` = 1 when built with the event trace (-DLLMFA_TRACE=1). Replaces
+ * `*trace` = the event-trace level (0 = none; 1 = event trace and segment
+ * timeline, -DLLMFA_TRACE=1; 2 = also per-wait-site statistics). Replaces
  * the reference's separate ladder kernels (scaffolding.cu with SKIP_SM_FULL,
  * faux.cu) and its ENABLE_PROF build flag (llm_fa.py:46-51), which it reports
  * nowhere at run time.
@@ -133,16 +134,17 @@ int llmfa_version(void);
 int llmfa_build_config(int* ablation, int* trace);
 
 /*
- * Event trace of the last launch (library built with -DLLMFA_TRACE=1 only;
- * otherwise returns LLMFA_ERR_UNSUPPORTED): copies the trace records
+ * Event trace of the last launch (library built with -DLLMFA_TRACE=1 or 2
+ * only; otherwise returns LLMFA_ERR_UNSUPPORTED): copies the trace records
  * ({uint64 globaltimer_ns, int64 clock64} per [cta rank][Q tile][event]
  * [iteration]) to host memory after synchronising the device, followed, when
  * `capacity_bytes` allows, by the per-cluster segment timeline (uint64
  * [160 clusters][32 segments][4]) and then by the per-wait-site statistics
- * of every launch since the last read (uint64 [16][2]: entry 0 = summed CTA
- * run time in SM cycles and the CTA count; entry s = %clock64 cycles lane 0 of
- * the waiting warps spent in the bounded waits of site s and their number),
- * which the read clears. Replaces the reference's
+ * of every launch since the last read (uint64 [16][2], all zero below level
+ * 2: entry 0 = summed CTA run time in SM cycles and the CTA count; entry s =
+ * the SM cycles that lane 0 of the waiting warps spent in those bounded waits
+ * of site s that took more than 64 cycles, and their number), which the read
+ * clears. Replaces the reference's
  * profiler ring flush (profiler.cuh:85-108) and the prof_buf / prof_count
  * outputs of llm_fa_forward (llm_fa.cu:1461-1474).
  */

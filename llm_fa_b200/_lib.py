@@ -107,7 +107,7 @@ def build_config(handle: ctypes.CDLL | None = None) -> dict:
     a, t = ctypes.c_int(-1), ctypes.c_int(-1)
     check(h.llmfa_build_config(ctypes.byref(a), ctypes.byref(t)), "llmfa_build_config")
     return {"ablation": a.value, "ablation_name": ABLATION_NAMES.get(a.value, str(a.value)),
-            "trace": bool(t.value)}
+            "trace": t.value}
 
 
 def error_string(code: int) -> str:

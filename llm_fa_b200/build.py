@@ -4,11 +4,13 @@ One nvcc invocation, no torch dependency in the binary (static cudart); the
 driver entry point for tensor-map encoding is resolved at run time, so the
 library builds on a machine without a GPU and loads on a machine with one.
 
-    python -m llm_fa_b200.build [--force] [-v] [--variant trace|floor|faux|noexp|all]
+    python -m llm_fa_b200.build [--force] [-v] [--variant NAME|all]
 
 Besides the product library, the same source builds variants (compile-time
 switches, each in its own library file, never loaded in place of the product):
-`trace` (-DLLMFA_TRACE=1: event trace and per-wait-site statistics) and the
+`trace` (-DLLMFA_TRACE=1: event trace and segment timeline), `waitstats`
+(-DLLMFA_TRACE=2: the trace plus per-wait-site statistics, which time every
+bounded wait and perturb the schedule more) and the
 ablation-ladder rungs `floor`, `faux`, `noexp` (-DLLMFA_ABLATE=1..3: the TMA +
 MMA floor, no softmax math, no exponentials; their output is not attention).
 """
@@ -46,6 +48,7 @@ def nvcc_path() -> str:
 # variant name -> extra nvcc defines
 VARIANTS = {
     "trace": ["-DLLMFA_TRACE=1"],
+    "waitstats": ["-DLLMFA_TRACE=2"],
     "floor": ["-DLLMFA_ABLATE=1"],
     "faux": ["-DLLMFA_ABLATE=2"],
     "noexp": ["-DLLMFA_ABLATE=3"],

@@ -7,7 +7,10 @@
 // rescaling of the O accumulator only when the running row maximum grows by
 // more than kRescaleThreshold (log2 units; the reference uses the same 8.0,
 // llm_fa.cu:857-866), and a final division by the row sum
-// (llm_fa.cu:1348-1406).
+// (llm_fa.cu:1348-1406). One deliberate difference: the row sum of each KV
+// tile also takes the bf16 rounding of the tile's largest probability, the
+// weight P V uses for it (the reference sums the fp32 probabilities only,
+// llm_fa.cu:1019-1031); see dominant_rounding.
 //
 // Work unit: 512 query rows of one (batch, head), processed by a cluster of
 // two CTAs (a CTA pair). The pair issues tcgen05 MMAs with cta_group::2 and
@@ -291,25 +294,37 @@ __device__ __forceinline__ bool mbar_wait_slow(uint32_t bar, uint32_t parity, co
   }
 }
 #if LLMFA_TRACE
-// Per-wait-site statistics of the attention kernel (trace builds only): lane 0
-// of every waiting warp adds the %clock64 cycles it spent in the wait and a
-// count to this CTA's slot of the site; the CTA's totals go to g_wait_stats at
-// teardown. Slot 0 holds the CTAs' own run time (cycles, CTA count).
+// Per-wait-site statistics of the attention kernel (LLMFA_TRACE=2 builds): lane
+// 0 of the waiting warp reads %clock before the wait's first probe and after
+// it completes; a wait that took more than kWaitFast cycles (one whose phase
+// had already completed returns within a few) adds its cycles and a count to
+// its own warp's slot of the site (plain shared-memory updates: each warp owns
+// its slots). The CTA's totals go to g_wait_stats at teardown; slot 0 holds
+// the CTAs' own run time (cycles, CTA count).
 constexpr int kWaitSlots = 16;
+constexpr uint32_t kWaitFast = 64;
+struct WaitSlot {
+  unsigned long long cycles;
+  unsigned long long count;
+};
 __device__ unsigned long long g_wait_stats[kWaitSlots * 2];
-__shared__ unsigned long long g_wait_acc[kWaitSlots * 2];
+#if LLMFA_TRACE >= 2
+__shared__ WaitSlot g_wait_slot[kThreads / 32][kWaitSlots];
+#endif
 #endif
 
 __device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, const WaitCtl& c,
                                           int site, bool honor_abort = true) {
-#if LLMFA_TRACE
+#if LLMFA_TRACE >= 2
   if (site <= kSiteDrain) {  // the attention kernel's sites (its prologue clears the slots)
-    const long long t0 = clock64();
+    const uint32_t t0 = static_cast<uint32_t>(clock());
     const bool ok = ptx::mbar_try_wait(bar, parity) ||
                     mbar_wait_slow(bar, parity, c, site, honor_abort);
-    if ((threadIdx.x & 31u) == 0) {
-      atomicAdd(&g_wait_acc[2 * site], static_cast<unsigned long long>(clock64() - t0));
-      atomicAdd(&g_wait_acc[2 * site + 1], 1ull);
+    const uint32_t dt = static_cast<uint32_t>(clock()) - t0;
+    if ((threadIdx.x & 31u) == 0 && dt > kWaitFast) {
+      WaitSlot& w = g_wait_slot[threadIdx.x >> 5][site];
+      w.cycles += dt;
+      w.count += 1ull;
     }
     return ok;
   }
@@ -537,6 +552,39 @@ __device__ __forceinline__ void exp_chunk(const uint32_t (&r)[32], uint64_t c2, 
   ptx::tmem_st16(t_p, pk);
 }
 
+// Whether a score equal to the row maximum `smax` sits in one of the columns
+// whose exp2 runs on the FMA pipe (kSoftmaxPolyMask) in this 32-column chunk.
+__device__ __forceinline__ bool max_in_poly_columns(const uint32_t (&r)[32], float smax) {
+  bool hit = false;
+#pragma unroll
+  for (int k = 0; k < 16; ++k)
+    if ((kSoftmaxPolyMask >> k) & 1u)
+      hit |= (__uint_as_float(r[2 * k]) == smax) | (__uint_as_float(r[2 * k + 1]) == smax);
+  return hit;
+}
+
+// bf16(p) - p for the tile's largest probability p = exp2(smax * scale*log2e - m),
+// computed exactly as exp_chunk computes that element (same fma, and the FMA-pipe
+// exp2 when the maximum sits in one of its columns). Added to the fp32 row sum it
+// makes the sum use the weight P V uses for the row's dominant key, so that a row
+// dominated by one key returns that key's V row without the key's bf16 rounding
+// error (up to 2^-9 relative, which bounds the max-abs error at logit ranges of
+// +-200); the other keys' rounding errors average out. Costs a few instructions
+// per row and tile instead of rounding every probability a second time.
+__device__ __forceinline__ float dominant_rounding(float smax, float scale_log2, float m,
+                                                   bool in_poly) {
+  const float x = fmaf(smax, scale_log2, -m);
+  float pm;
+  if constexpr (kAblate == 3) {
+    pm = x;
+  } else {
+    float p0, p1;
+    ptx::f2_unpack(exp2_poly_x2(ptx::f2_pack(x, x)), p0, p1);
+    pm = in_poly ? p0 : ptx::ex2_mufu(x);
+  }
+  return __uint_as_float(ptx::bf16x2_pack(pm, 0.f) << 16) - pm;
+}
+
 // kWithLse: also write the per-row log-sum-exp (FwdParams::lse). A separate
 // instantiation, so the plain forward's code is not touched by it (the
 // correction warps' register allocation moved the plain path by ~3%).
@@ -591,9 +639,10 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
     g_cta_abort = 0u;
     ptx::fence_mbar_init();
   }
-#if LLMFA_TRACE
+#if LLMFA_TRACE >= 2
   const long long cta_t0 = clock64();
-  if (threadIdx.x < 2 * kWaitSlots) g_wait_acc[threadIdx.x] = 0ull;
+  if (threadIdx.x < (kThreads / 32) * kWaitSlots)
+    (&g_wait_slot[0][0])[threadIdx.x] = WaitSlot{0ull, 0ull};
 #endif
   if (warp == 12) {
     ptx::tmem_alloc<2>(smem_base + kSmemTmemSlot, 512);
@@ -655,7 +704,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
         // TMEM in pass 2 behind the exponentials of chunks 0-1, which keeps
         // the live set small enough for the softmax register budget.
         uint32_t s0[32], s1[32];
-        float mt;
+        float mt, smax;
+        bool max_poly = false;
         {
           uint32_t s2[32], s3[32];
           ptx::tmem_ld32(t_s + 0, s0);
@@ -674,11 +724,15 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
             mask_tail(s2, 64, p.kv_tail);
             mask_tail(s3, 96, p.kv_tail);
           }
-          if constexpr (kAblate == 2)  // faux: no row max
+          if constexpr (kAblate == 2) {  // faux: no row max
+            smax = 0.f;
             mt = 0.f;
-          else
-            mt = fmaxf(fmaxf(chunk_max(s0), chunk_max(s1)), fmaxf(chunk_max(s2), chunk_max(s3))) *
-                 p.scale_log2;
+          } else {
+            smax = fmaxf(fmaxf(chunk_max(s0), chunk_max(s1)), fmaxf(chunk_max(s2), chunk_max(s3)));
+            mt = smax * p.scale_log2;
+            max_poly = max_in_poly_columns(s0, smax) | max_in_poly_columns(s1, smax) |
+                       max_in_poly_columns(s2, smax) | max_in_poly_columns(s3, smax);
+          }
         }
         float sc = 1.f;
         if (j == 0) {
@@ -720,7 +774,10 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
         }
         float l0, l1;
         ptx::f2_unpack(ptx::f2_add(lsum_a, lsum_b), l0, l1);
-        l += l0 + l1;
+        if constexpr (kAblate == 2)
+          l += l0 + l1;
+        else
+          l += l0 + l1 + dominant_rounding(smax, p.scale_log2, m, max_poly);
         ptx::tmem_wait_st();
         ptx::tc_fence_before();
         __syncwarp();
@@ -1214,13 +1271,21 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
   asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
   ptx::tc_fence_before();
   __syncthreads();
-#if LLMFA_TRACE
-  if (threadIdx.x == 0) {
-    g_wait_acc[0] = static_cast<unsigned long long>(clock64() - cta_t0);
-    g_wait_acc[1] = 1ull;
+#if LLMFA_TRACE >= 2
+  if (threadIdx.x < kWaitSlots) {
+    unsigned long long cyc = 0, cnt = 0;
+    if (threadIdx.x == 0) {
+      cyc = static_cast<unsigned long long>(clock64() - cta_t0);
+      cnt = 1;
+    } else {
+      for (int w = 0; w < kThreads / 32; ++w) {
+        cyc += g_wait_slot[w][threadIdx.x].cycles;
+        cnt += g_wait_slot[w][threadIdx.x].count;
+      }
+    }
+    atomicAdd(&g_wait_stats[2 * threadIdx.x], cyc);
+    atomicAdd(&g_wait_stats[2 * threadIdx.x + 1], cnt);
   }
-  __syncthreads();
-  if (threadIdx.x < 2 * kWaitSlots) atomicAdd(&g_wait_stats[threadIdx.x], g_wait_acc[threadIdx.x]);
 #endif
   ptx::cluster_sync();
   if (warp == 12) {

@@ -16,6 +16,7 @@
 #include <cmath>
 #include <cstdint>
 #include <cstdlib>
+#include <cstring>
 #include <mutex>
 
 #include "../../include/llm_fa_b200.h"
@@ -277,6 +278,160 @@ int check_forward_args(const void* q, const int64_t q_strides[3], const void* k,
   return LLMFA_OK;
 }
 
+// Everything that determines the tensor maps and the launch plan of a call.
+struct LaunchKey {
+  const void *q, *k, *v, *o, *ws;
+  const float* lse;
+  int64_t qs[3], ks[3], vs[3], os[3], ls[2];
+  int64_t batch, heads, seq_q, seq_k;
+  uint64_t ws_bytes;
+  uint32_t scale_bits;
+};
+
+// What one forward launches: the attention kernel's tensor maps and
+// parameters, and the combine kernel's parameters when KV ranges are split.
+struct LaunchSpec {
+  CUtensorMap tq, tk, tv, to, tw;
+  llmfa::FwdParams p;
+  llmfa::CombineParams cp;
+  int nclusters;
+  bool combine;
+};
+
+// A few recent launch specs per device (round-robin replacement), so that a
+// loop of calls on the same buffers skips the tensor-map encoding and the
+// stream-K planning (host time that bounds small shapes).
+class LaunchCache {
+ public:
+  bool lookup(const LaunchKey& key, LaunchSpec& out) {
+    std::lock_guard<std::mutex> lock(mu_);
+    for (int i = 0; i < kEntries; ++i) {
+      if (valid_[i] && std::memcmp(&keys_[i], &key, sizeof(LaunchKey)) == 0) {
+        out = specs_[i];
+        return true;
+      }
+    }
+    return false;
+  }
+  void insert(const LaunchKey& key, const LaunchSpec& spec) {
+    std::lock_guard<std::mutex> lock(mu_);
+    keys_[next_] = key;
+    specs_[next_] = spec;
+    valid_[next_] = true;
+    next_ = (next_ + 1) % kEntries;
+  }
+
+ private:
+  static constexpr int kEntries = 8;
+  std::mutex mu_;
+  LaunchKey keys_[kEntries];
+  LaunchSpec specs_[kEntries];
+  bool valid_[kEntries] = {};
+  int next_ = 0;
+};
+LaunchCache g_cache[kMaxDevices];
+
+// Encodes the tensor maps and plans the launch (persistent clusters, stream-K
+// cut and the combine kernel's piece table) for checked arguments.
+int make_launch_spec(const LaunchKey& a, const DeviceSetup& s, LaunchSpec& spec) {
+  int rc;
+  if ((rc = encode_bshd(&spec.tq, a.q, a.qs, a.seq_q, a.heads, a.batch, llmfa::kBlockM)) != LLMFA_OK)
+    return rc;
+  if ((rc = encode_bshd(&spec.tk, a.k, a.ks, a.seq_k, a.heads, a.batch,
+                        llmfa::kBlockN / llmfa::kPair)) != LLMFA_OK)
+    return rc;
+  if ((rc = encode_bshd(&spec.tv, a.v, a.vs, a.seq_k, a.heads, a.batch, llmfa::kBlockN)) != LLMFA_OK)
+    return rc;
+  if ((rc = encode_bshd(&spec.to, a.o, a.os, a.seq_q, a.heads, a.batch, llmfa::kBlockM)) != LLMFA_OK)
+    return rc;
+
+  llmfa::FwdParams& p = spec.p;
+  p = llmfa::FwdParams{};
+  const int64_t n_qblk = (a.seq_q + llmfa::kUnitRows - 1) / llmfa::kUnitRows;
+  float scale;
+  std::memcpy(&scale, &a.scale_bits, sizeof(float));
+  p.B = static_cast<int>(a.batch);
+  p.H = static_cast<int>(a.heads);
+  p.Sq = static_cast<int>(a.seq_q);
+  p.Sk = static_cast<int>(a.seq_k);
+  p.n_qblk = static_cast<int>(n_qblk);
+  p.n_kv = static_cast<int>((a.seq_k + llmfa::kBlockN - 1) / llmfa::kBlockN);
+  p.n_units = static_cast<int>(a.batch * a.heads * n_qblk);
+  p.kv_tail = static_cast<int>(a.seq_k - int64_t(p.n_kv - 1) * llmfa::kBlockN);
+  p.scale_log2 = scale * 1.4426950408889634f;
+  p.lse = const_cast<float*>(a.lse);
+  p.lse_sb = a.lse != nullptr ? a.ls[0] : 0;
+  p.lse_sh = a.lse != nullptr ? a.ls[1] : 0;
+  p.wait.timeout_ns = wait_timeout_ns();
+  p.wait.status = s.status_ptr;
+
+  const int G = s.max_clusters;
+  const uint64_t need = static_cast<uint64_t>(2 * G) * llmfa::kSlotBytes;
+  spec.nclusters =
+      llmfa::make_plan(p, G, a.ws != nullptr && a.ws_bytes >= need && aligned16(a.ws));
+  spec.combine = false;
+  spec.cp = llmfa::CombineParams{};
+  if (p.sk_mode) {
+    p.ws_ml = reinterpret_cast<float*>(static_cast<char*>(const_cast<void*>(a.ws)) +
+                                       static_cast<uint64_t>(2 * G) * llmfa::kSlotOBytes);
+    // the O parts of all slots as one [2G * 512, 128] bf16 matrix
+    const int64_t ws_rows = int64_t(2 * G) * llmfa::kSlotRows;
+    const int64_t ws_strides[3] = {ws_rows * 128, 128, 128};
+    if ((rc = encode_bshd(&spec.tw, a.ws, ws_strides, ws_rows, 1, 1, llmfa::kBlockM)) != LLMFA_OK)
+      return rc;
+    llmfa::CombineParams& cp = spec.cp;
+    cp.ws_o = static_cast<const uint16_t*>(a.ws);
+    cp.ws_ml = p.ws_ml;
+    cp.o = static_cast<uint16_t*>(const_cast<void*>(a.o));
+    cp.o_sb = a.os[0];
+    cp.o_ss = a.os[1];
+    cp.o_sh = a.os[2];
+    cp.lse = p.lse;
+    cp.lse_sb = p.lse_sb;
+    cp.lse_sh = p.lse_sh;
+    cp.wait = p.wait;
+    cp.H = p.H;
+    cp.Sq = p.Sq;
+    cp.n_qblk = p.n_qblk;
+    cp.n_split = list_split_units(p, &cp);
+    spec.combine = cp.n_split > 0;
+  } else {
+    spec.tw = spec.to;  // not read without split units
+  }
+  return LLMFA_OK;
+}
+
+int launch_spec(const LaunchSpec& spec, cudaStream_t st) {
+  const dim3 grid(2 * spec.nclusters, 1, 1), block(llmfa::kThreads, 1, 1);
+  if (spec.p.lse != nullptr)
+    llmfa::llm_fa_kernel_sm100<true><<<grid, block, llmfa::kSmemBytes, st>>>(
+        spec.tq, spec.tk, spec.tv, spec.to, spec.tw, spec.p);
+  else
+    llmfa::llm_fa_kernel_sm100<false><<<grid, block, llmfa::kSmemBytes, st>>>(
+        spec.tq, spec.tk, spec.tv, spec.to, spec.tw, spec.p);
+  if (cudaGetLastError() != cudaSuccess) return LLMFA_ERR_LAUNCH;
+  if (spec.combine) {
+    cudaLaunchConfig_t cfg{};
+    cfg.gridDim = dim3(spec.cp.n_split * llmfa::kCombineBlocksPerUnit);
+    cfg.blockDim = dim3(llmfa::kCombineThreads);
+    cfg.dynamicSmemBytes = static_cast<size_t>(spec.cp.round_pieces) * llmfa::kCombinePieceBytes;
+    cfg.stream = st;
+    // Programmatic dependent launch: the combine grid is scheduled while the
+    // attention kernel's last CTAs finish and waits (griddepcontrol.wait)
+    // for that kernel's completion before reading the partial results.
+    cudaLaunchAttribute attr{};
+    attr.id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr.val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = &attr;
+    cfg.numAttrs = 1;
+    if (cudaLaunchKernelEx(&cfg, llmfa::llm_fa_combine_kernel, spec.cp) != cudaSuccess) {
+      cudaGetLastError();
+      return LLMFA_ERR_LAUNCH;
+    }
+  }
+  return LLMFA_OK;
+}
+
 }  // namespace
 
 extern "C" {
@@ -291,100 +446,32 @@ int llmfa_forward_lse(const void* q, const int64_t q_strides[3], const void* k,
   int rc = check_forward_args(q, q_strides, k, k_strides, v, v_strides, o, o_strides, lse,
                               lse_strides, batch, heads, seq_q, seq_k, softmax_scale);
   if (rc != LLMFA_OK) return rc;
-  const int64_t n_qblk = (seq_q + llmfa::kUnitRows - 1) / llmfa::kUnitRows;
-  const int64_t n_units = batch * heads * n_qblk;
-
   int dev = 0;
   DeviceSetup* s = nullptr;
   if ((rc = device_setup(&dev, &s)) != LLMFA_OK) return rc;
 
-  CUtensorMap tq, tk, tv, to, tw;
-  if ((rc = encode_bshd(&tq, q, q_strides, seq_q, heads, batch, llmfa::kBlockM)) != LLMFA_OK)
-    return rc;
-  if ((rc = encode_bshd(&tk, k, k_strides, seq_k, heads, batch, llmfa::kBlockN / llmfa::kPair)) !=
-      LLMFA_OK)
-    return rc;
-  if ((rc = encode_bshd(&tv, v, v_strides, seq_k, heads, batch, llmfa::kBlockN)) != LLMFA_OK)
-    return rc;
-  if ((rc = encode_bshd(&to, o, o_strides, seq_q, heads, batch, llmfa::kBlockM)) != LLMFA_OK)
-    return rc;
-
-  llmfa::FwdParams p{};
-  p.B = static_cast<int>(batch);
-  p.H = static_cast<int>(heads);
-  p.Sq = static_cast<int>(seq_q);
-  p.Sk = static_cast<int>(seq_k);
-  p.n_qblk = static_cast<int>(n_qblk);
-  p.n_kv = static_cast<int>((seq_k + llmfa::kBlockN - 1) / llmfa::kBlockN);
-  p.n_units = static_cast<int>(n_units);
-  p.kv_tail = static_cast<int>(seq_k - int64_t(p.n_kv - 1) * llmfa::kBlockN);
-  p.scale_log2 = softmax_scale * 1.4426950408889634f;
-  p.lse = lse;
-  p.lse_sb = lse != nullptr ? lse_strides[0] : 0;
-  p.lse_sh = lse != nullptr ? lse_strides[1] : 0;
-  p.wait.timeout_ns = wait_timeout_ns();
-  p.wait.status = s->status_ptr;
-
-  const int G = s->max_clusters;
-  const uint64_t need = static_cast<uint64_t>(2 * G) * llmfa::kSlotBytes;
-  const int nclusters =
-      llmfa::make_plan(p, G, workspace != nullptr && workspace_bytes >= need && aligned16(workspace));
-  if (p.sk_mode) {
-    p.ws_ml = reinterpret_cast<float*>(static_cast<char*>(workspace) +
-                                       static_cast<uint64_t>(2 * G) * llmfa::kSlotOBytes);
-    // the O parts of all slots as one [2G * 512, 128] bf16 matrix
-    const int64_t ws_rows = int64_t(2 * G) * llmfa::kSlotRows;
-    const int64_t ws_strides[3] = {ws_rows * 128, 128, 128};
-    if ((rc = encode_bshd(&tw, workspace, ws_strides, ws_rows, 1, 1, llmfa::kBlockM)) != LLMFA_OK)
-      return rc;
-  } else {
-    tw = to;  // not read without split units
+  // Tensor maps and launch plan depend only on the arguments: repeated calls
+  // with the same buffers and sizes reuse them (LaunchCache).
+  LaunchKey key;
+  std::memset(&key, 0, sizeof(key));  // padding too: keys compare bytewise
+  key.q = q; key.k = k; key.v = v; key.o = o; key.lse = lse; key.ws = workspace;
+  for (int i = 0; i < 3; ++i) {
+    key.qs[i] = q_strides[i]; key.ks[i] = k_strides[i];
+    key.vs[i] = v_strides[i]; key.os[i] = o_strides[i];
   }
-  cudaStream_t st = static_cast<cudaStream_t>(stream);
-  if (p.lse != nullptr)
-    llmfa::llm_fa_kernel_sm100<true><<<dim3(2 * nclusters, 1, 1), dim3(llmfa::kThreads, 1, 1),
-                                       llmfa::kSmemBytes, st>>>(tq, tk, tv, to, tw, p);
-  else
-    llmfa::llm_fa_kernel_sm100<false><<<dim3(2 * nclusters, 1, 1), dim3(llmfa::kThreads, 1, 1),
-                                        llmfa::kSmemBytes, st>>>(tq, tk, tv, to, tw, p);
-  if (cudaGetLastError() != cudaSuccess) return LLMFA_ERR_LAUNCH;
-  if (p.sk_mode) {
-    llmfa::CombineParams cp{};
-    cp.ws_o = static_cast<const uint16_t*>(workspace);
-    cp.ws_ml = p.ws_ml;
-    cp.o = static_cast<uint16_t*>(o);
-    cp.o_sb = o_strides[0];
-    cp.o_ss = o_strides[1];
-    cp.o_sh = o_strides[2];
-    cp.lse = p.lse;
-    cp.lse_sb = p.lse_sb;
-    cp.lse_sh = p.lse_sh;
-    cp.wait = p.wait;
-    cp.H = p.H;
-    cp.Sq = p.Sq;
-    cp.n_qblk = p.n_qblk;
-    cp.n_split = list_split_units(p, &cp);
-    if (cp.n_split > 0) {
-      cudaLaunchConfig_t cfg{};
-      cfg.gridDim = dim3(cp.n_split * llmfa::kCombineBlocksPerUnit);
-      cfg.blockDim = dim3(llmfa::kCombineThreads);
-      cfg.dynamicSmemBytes = static_cast<size_t>(cp.round_pieces) * llmfa::kCombinePieceBytes;
-      cfg.stream = st;
-      // Programmatic dependent launch: the combine grid is scheduled while the
-      // attention kernel's last CTAs finish and waits (griddepcontrol.wait)
-      // for that kernel's completion before reading the partial results.
-      cudaLaunchAttribute attr{};
-      attr.id = cudaLaunchAttributeProgrammaticStreamSerialization;
-      attr.val.programmaticStreamSerializationAllowed = 1;
-      cfg.attrs = &attr;
-      cfg.numAttrs = 1;
-      if (cudaLaunchKernelEx(&cfg, llmfa::llm_fa_combine_kernel, cp) != cudaSuccess) {
-        cudaGetLastError();
-        return LLMFA_ERR_LAUNCH;
-      }
-    }
+  if (lse != nullptr) { key.ls[0] = lse_strides[0]; key.ls[1] = lse_strides[1]; }
+  key.batch = batch; key.heads = heads; key.seq_q = seq_q; key.seq_k = seq_k;
+  std::memcpy(&key.scale_bits, &softmax_scale, sizeof(float));
+  key.ws_bytes = workspace_bytes;
+
+  LaunchSpec spec;
+  if (!g_cache[dev].lookup(key, spec)) {
+    if ((rc = make_launch_spec(key, *s, spec)) != LLMFA_OK) return rc;
+    g_cache[dev].insert(key, spec);
   }
-  return LLMFA_OK;
+  spec.p.wait.timeout_ns = wait_timeout_ns();  // may change between calls
+  spec.cp.wait = spec.p.wait;
+  return launch_spec(spec, static_cast<cudaStream_t>(stream));
 }
 
 int llmfa_forward_2d(const void* q, const void* k, const void* v, void* o, int64_t seq_q,

@@ -14,24 +14,30 @@ product library:
     noexp   the full softmax with exp2(x) replaced by x
     full    the product
 
-Every rung runs the same launch plan on the same inputs; each timed call is
-bracketed by CUDA events after a 256 MiB L2 flush, rungs take turns within
-each round, and the median per rung is reported (ms, TFLOP/s and the time the
-rung adds over the previous one). The rungs' outputs are not attention: this
-is a measurement tool, never a product path (bench.py refuses a library built
-with an ablation switch).
+Every rung runs the same launch plan on the same inputs, timed as bench.py
+times the product: each call bracketed by CUDA events after a 256 MiB L2
+flush, all calls of a block queued before one synchronisation. Rungs take
+turns block by block, each block after a short idle pause and its own
+warm-up calls (so that no rung inherits another's power state), and the
+median per rung is reported (ms,
+TFLOP/s and the time the rung adds over the previous one), with the SM clocks
+sampled over the whole run. The rungs' outputs are not attention: this is a
+measurement tool, never a product path (bench.py refuses a library built with
+an ablation switch).
 """
 from __future__ import annotations
 
 import argparse
 import json
 import statistics
+import time
 
 import torch
 
 from . import _lib
 from .attention import forward_with
 from .build import build_variant
+from .gpuclocks import ClockSampler
 
 RUNGS = ["floor", "faux", "noexp", "full"]
 EXPECTED = {"floor": 1, "faux": 2, "noexp": 3, "full": 0}
@@ -65,26 +71,32 @@ def main() -> None:
     flush = torch.empty(256 << 20, dtype=torch.uint8, device=dev)
 
     def timed(h) -> list[float]:
-        ts = []
-        for i in range(a.warmup + a.steps):
+        time.sleep(0.1)
+        for _ in range(a.warmup):
             flush.zero_()
-            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            forward_with(h, q, k, v, out=o)
+        ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+              for _ in range(a.steps)]
+        for e0, e1 in ev:
+            flush.zero_()  # ~70 us on the GPU: covers the host's launch of the next call
             e0.record()
             forward_with(h, q, k, v, out=o)
             e1.record()
-            torch.cuda.synchronize()
-            if i >= a.warmup:
-                ts.append(e0.elapsed_time(e1))
-        return ts
+        torch.cuda.synchronize()
+        return [e0.elapsed_time(e1) for e0, e1 in ev]
 
     times = {name: [] for name in RUNGS}
+    sampler = ClockSampler(dev.index)
+    sampler.start()
     for _ in range(a.rounds):
         for name in RUNGS:
             times[name] += timed(handles[name])
+    clocks = sampler.stop()
     for name, h in handles.items():
         st = ctypes_status(h)
         if st != 0:
             raise RuntimeError(f"rung {name}: device status {st:#x}")
+    print(json.dumps({"config": cfg.name, "clocks": clocks}), flush=True)
     prev = None
     for name in RUNGS:
         ms = statistics.median(times[name])

@@ -92,8 +92,9 @@ def read_segments(handle=None) -> np.ndarray:
 
 
 def wait_table(wait: np.ndarray, clock_ghz: float) -> list[dict]:
-    """Per wait site: waits per CTA, mean wait, and the share of the waiting warps' time
-    spent there (cycles waited / (warps of the role x CTA run cycles))."""
+    """Per wait site, over the waits that took more than 64 cycles: how many per CTA, their
+    mean length, and the share of the waiting warps' time spent in them (cycles waited /
+    (warps of the role x CTA run cycles))."""
     cta_cycles, ctas = float(wait[0, 0]), max(float(wait[0, 1]), 1.0)
     rows = []
     for site, (role, what) in WAIT_SITES.items():
@@ -251,9 +252,9 @@ def to_chrome_json(tr: np.ndarray, path: str, clock_ghz: float) -> None:
 
 
 def main() -> None:
-    """python -m llm_fa_b200.trace [--config c3] [--chrome out.json]: build the trace
-    variant, run the configuration through it, and print the per-hop latencies, the
-    hand-off chain check and the per-wait-site table (markdown)."""
+    """python -m llm_fa_b200.trace [--config c3] [--chrome out.json]: run the configuration
+    through the trace build (hand-off latencies, chain check) and the wait-statistics build
+    (per-wait-site table, markdown), with each build's time beside the product's."""
     import argparse
 
     import torch
@@ -267,37 +268,45 @@ def main() -> None:
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--chrome", default=None, help="write a Chrome trace-event JSON here")
     a = ap.parse_args()
-    h = _lib.load(build_variant("trace"))
-    if not _lib.build_config(h)["trace"]:
-        raise RuntimeError("trace variant built without LLMFA_TRACE")
+    builds = {"product": _lib.lib(), "trace": _lib.load(build_variant("trace")),
+              "waitstats": _lib.load(build_variant("waitstats"))}
     cfg = CONFIGS[a.config]
     dev = torch.device("cuda", 0)
     q, k, v = (t.to(dev) for t in make_inputs(cfg))
     o = torch.empty_like(q)
-    for _ in range(a.warmup):
+    flush = torch.empty(256 << 20, dtype=torch.uint8, device=dev)
+    got = {}
+    for name, h in builds.items():
+        for _ in range(a.warmup):
+            forward_with(h, q, k, v, out=o)
+        torch.cuda.synchronize()
+        if name != "product":
+            read_all(h)  # clears the wait statistics of the warm-up launches
+        flush.zero_()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
         forward_with(h, q, k, v, out=o)
-    torch.cuda.synchronize()
-    read_all(h)  # clears the wait statistics of the warm-up launches
-    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    e0.record()
-    forward_with(h, q, k, v, out=o)
-    e1.record()
-    torch.cuda.synchronize()
-    ev, seg, wait = read_all(h)
+        e1.record()
+        torch.cuda.synchronize()
+        got[name] = (e0.elapsed_time(e1), None if name == "product" else read_all(h))
+    print(f"# {cfg.name} ({cfg.describe()}): " + ", ".join(
+        f"{n} build {t:.3f} ms" for n, (t, _) in got.items()))
+    ev = got["trace"][1][0]
     ghz = clock_ghz(ev)
-    print(f"# trace build, {cfg.name} ({cfg.describe()}): {e0.elapsed_time(e1):.3f} ms, "
-          f"SM clock {ghz:.3f} GHz (from the trace)")
-    print("\n## hand-off latencies (median over the traced window, ns)\n")
+    print(f"# SM clock from the trace: {ghz:.3f} GHz")
+    print("\n## hand-off latencies of the trace build (median over the traced window, ns)\n")
     for name, val in hop_latencies(ev, ghz).items():
         print(f"- {name}: {val:.0f}")
     bad = check_chain(ev)
     print(f"\n## chain check: {'ok' if not bad else f'{len(bad)} violations'}")
     for b in bad[:20]:
         print(f"- {b}")
-    print("\n## wait sites (all CTAs of the launch)\n")
+    ev2, _, wait = got["waitstats"][1]
+    print("\n## wait sites of the wait-statistics build (all CTAs of the launch; waits longer "
+          "than 64 cycles)\n")
     print("| site | role | waits for | waits per CTA | mean wait (ns) | share of the role's time |")
     print("|---|---|---|---|---|---|")
-    for r in wait_table(wait, ghz):
+    for r in wait_table(wait, clock_ghz(ev2)):
         print(f"| {r['site']} | {r['role']} | {r['waits_for']} | {r['waits_per_cta']:.1f} | "
               f"{r['mean_wait_ns']:.0f} | {100 * r['share_of_role_time']:.1f} % |")
     if a.chrome:

@@ -8,7 +8,7 @@ bf16. For the softmax-stress configuration, after the three draws, q and then
 k get round(0.05*S) rows per (batch, head) multiplied by 4, the rows chosen by
 `torch.randperm(S)` from the same generator (batch-major, head-minor order).
 No public dataset is involved; these stand in for the reference's random
-single-head inputs (bench.py:63-76) at the BASELINE shapes.
+single-head inputs (bench.py:63-76) at the benchmark configurations' shapes.
 """
 from __future__ import annotations
 
@@ -47,7 +47,7 @@ class Config:
                 f"seed{self.seed}{' stress' if self.stress_rows else ''}")
 
 
-# BASELINE.json "configs", in order.
+# The benchmark configurations c1..c5, in order.
 CONFIGS = {
     "c1": Config("c1", 1, 2, 1024, 1024, seed=0),
     "c2": Config("c2", 1, 1, 16384, 16384, seed=1),

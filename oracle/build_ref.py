@@ -1,6 +1,6 @@
 """Build the reference's kernels from their own sources into oracle/_ref/.
 
-TEST/BASELINE INFRASTRUCTURE ONLY. The reference's path is one CUDA file plus
+TEST AND COMPARISON INFRASTRUCTURE ONLY. The reference's path is one CUDA file plus
 one header (llm_fa.cu, profiler.cuh) compiled as a torch extension with the
 flags of llm_fa.py:46-51; its ablation-ladder kernels scaffolding.cu and
 faux.cu (scaffolding.py, faux.py) are built the same way. This recipe compiles

@@ -11,7 +11,7 @@ softmax(Q K^T * scale) V with an online softmax (llm_fa.cu:805-1060,
 1348-1406). Two restatements are kept:
 
 * `sdpa_fp32` — torch SDPA on the CPU in fp32 on bf16-rounded inputs: the
-  reference's own oracle path, run on host cores (BASELINE config 1);
+  reference's own oracle path, run on host cores (configuration c1's method);
 * `attention_np` — an independent numpy restatement of the math
   (max-subtracted exp, row sum, divide) in float64, used to pin `sdpa_fp32`.
 
@@ -73,6 +73,6 @@ def compare(out: torch.Tensor, ref: torch.Tensor) -> dict:
             "nonfinite": int((~torch.isfinite(out.float().cpu())).sum())}
 
 
-# Tolerances on O: max-abs 2e-2, mean-abs 2e-3.
+# Parity tolerances on O: max-abs 2e-2, mean-abs 2e-3.
 MAX_ABS_TOL = 2e-2
 MEAN_ABS_TOL = 2e-3

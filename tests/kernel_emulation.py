@@ -5,7 +5,9 @@ head): 128-key tiles; row max of the raw scores times scale*log2(e); lazy
 rescale only when the max grows by more than 8 (log2 units); exponentials
 exp2(s*c - m) with the columns the kernel sends to the FMA-pipe polynomial
 evaluated by the same polynomial (softmax_exp2.cuh); P rounded to bf16
-before P@V; fp32 row sums of the unrounded exponentials; final O/l in bf16.
+before P@V; fp32 row sums of the exponentials plus, per tile, the bf16
+rounding of the tile's largest one (computed as the kernel computes that
+element); final O/l in bf16.
 Lets the CPU suite check the algorithm (and the polynomial) against the
 oracle without a GPU.
 """
@@ -92,6 +94,12 @@ def attention_kernel_emulation(q: np.ndarray, k: np.ndarray, v: np.ndarray,
         e = np.exp2(x).astype(np.float32)
         e[:, polyc] = exp2_poly(x[:, polyc])
         l = (l + e.sum(axis=1, dtype=np.float32)).astype(np.float32)
+        # the bf16 rounding of each row's largest probability of the tile (dominant_rounding)
+        smax = s.max(axis=1)
+        xmax = _fma32(smax, np.full_like(smax, c), -m)
+        in_poly = (s[:, polyc] == smax[:, None]).any(axis=1)
+        pm = np.where(in_poly, exp2_poly(xmax), np.exp2(xmax)).astype(np.float32)
+        l = (l + (bf16_round(pm) - pm)).astype(np.float32)
         p = bf16_round(e)
         vpad = np.zeros((128, D), np.float32)
         vpad[:vt.shape[0]] = vt

@@ -125,7 +125,7 @@ def test_python_wrapper_rejects_cpu_tensors():
 def test_product_build_has_no_ablation_or_trace(L):
     """The default library is the product: no ablation-ladder rung, no event trace."""
     cfg = _lib.build_config(L)
-    assert cfg == {"ablation": 0, "ablation_name": "none", "trace": False}
+    assert cfg == {"ablation": 0, "ablation_name": "none", "trace": 0}
     a, t = ctypes.c_int(-1), ctypes.c_int(-1)
     assert L.llmfa_build_config(None, ctypes.byref(t)) == _lib.LLMFA_ERR_INVALID_ARGUMENT
     assert L.llmfa_build_config(ctypes.byref(a), ctypes.byref(t)) == _lib.LLMFA_OK
@@ -135,7 +135,7 @@ def test_ablation_variant_reports_its_rung():
     """A ladder rung is a separate library file that says what it is (no GPU needed)."""
     from llm_fa_b200.build import build_variant
     h = _lib.load(build_variant("floor"))
-    assert _lib.build_config(h) == {"ablation": 1, "ablation_name": "floor", "trace": False}
+    assert _lib.build_config(h) == {"ablation": 1, "ablation_name": "floor", "trace": 0}
 
 
 def test_bench_refuses_an_ablation_build(monkeypatch):
@@ -148,7 +148,7 @@ def test_bench_refuses_an_ablation_build(monkeypatch):
     import bench
     from llm_fa_b200.workloads import CONFIGS
     monkeypatch.setattr(llm_fa_b200, "build_info",
-                        lambda: {"ablation": 1, "ablation_name": "floor", "trace": False})
+                        lambda: {"ablation": 1, "ablation_name": "floor", "trace": 0})
     args = argparse.Namespace(warmup=3, steps=1, no_e2e=True, no_cpu_baseline=True,
                               validate=False, cpu_seconds=1.0)
     with pytest.raises(RuntimeError, match="ablation"):

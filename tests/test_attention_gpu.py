@@ -1,8 +1,8 @@
 """GPU parity tests of the sm_100a kernel through the C ABI.
 
 Reference semantics: fp32 SDPA on bf16-rounded inputs (validate.py:19-27);
-tolerance on O: max-abs 2e-2, mean-abs 2e-3. At the
-BASELINE sizes the CPU oracle checks a seeded subset of query rows (rows are
+tolerance on O: max-abs 2e-2, mean-abs 2e-3. At the benchmark
+configurations' sizes the CPU oracle checks a seeded subset of query rows (rows are
 independent), a chunked GPU fp32 SDPA checks every row, and size-independent
 properties (K/V permutation invariance, linearity in V, constant V) are
 checked on the full output.
@@ -342,7 +342,7 @@ def test_mirror_module_surface():
     assert out[0].shape == (512, 128)
 
 
-# ----------------------------------------------------------------- BASELINE sizes
+# ----------------------------------------------------------------- benchmark configurations
 def _sampled_parity(cfg, nrows, heads=None):
     q, k, v = make_inputs(cfg)
     o = attention_forward(q.cuda(), k.cuda(), v.cuda())

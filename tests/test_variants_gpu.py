@@ -5,8 +5,8 @@
   follow the per-tile chain S(j) visible -> scores loaded -> rescale factor ->
   P half -> MMA sees P half / P full -> QK(j+1) -> S(j+1) visible: the
   verification the reference runs on its own traces (its trace conventions'
-  checklist and its flow walker). Its per-wait-site counts match the number
-  of hand-offs the schedule implies.
+  checklist and its flow walker). The wait-statistics build (trace level 2)
+  reports per-wait-site statistics within the hand-offs the schedule has.
 * The ablation-ladder rungs (floor, faux, noexp) run to completion with a clean
   device status; their outputs are not attention and are not checked.
 """
@@ -31,12 +31,7 @@ def _status(h) -> int:
     return out.value
 
 
-def test_trace_build_events_chain_and_wait_counts():
-    h = _lib.load(build_variant("trace"))
-    assert _lib.build_config(h) == {"ablation": 0, "ablation_name": "none", "trace": True}
-    # 2 query blocks x 64 KV tiles, classic schedule (no workspace): cluster 0 runs unit 0
-    # over all 64 tiles, which covers the traced iterations 32..47
-    cfg = Config("tr", 1, 1, 1024, 8192, seed=77)
+def _traced_forward(h, cfg):
     q, k, v = make_inputs(cfg)
     qd, kd, vd = q.cuda(), k.cuda(), v.cuda()
     forward_with(h, qd, kd, vd, split_kv=False)  # warm-up
@@ -48,8 +43,18 @@ def test_trace_build_events_chain_and_wait_counts():
     err = compare(o, sdpa_fp32(q, k, v))
     assert err["nonfinite"] == 0
     assert err["max_abs"] < MAX_ABS_TOL and err["mean_abs"] < MEAN_ABS_TOL, err
+    return trace.read_all(h)
 
-    ev, seg, wait = trace.read_all(h)
+
+# 2 query blocks x 64 KV tiles, classic schedule (no workspace): cluster 0 runs unit 0 over
+# all 64 tiles, which covers the traced iterations 32..47
+TRACE_CFG = Config("tr", 1, 1, 1024, 8192, seed=77)
+
+
+def test_trace_build_events_and_chain():
+    h = _lib.load(build_variant("trace"))
+    assert _lib.build_config(h) == {"ablation": 0, "ablation_name": "none", "trace": 1}
+    ev, seg, wait = _traced_forward(h, TRACE_CFG)
     assert trace.check_chain(ev) == []
     E = {e: i for i, e in enumerate(trace.EVENTS)}
     for name in ("s_ready", "stat", "p_half", "p_full", "corr_stat", "corr_p_full", "prod_load"):
@@ -57,18 +62,28 @@ def test_trace_build_events_chain_and_wait_counts():
             assert (ev[r, :, E[name]]["globaltimer_ns"] > 0).all(), (name, r)
     for name in ("mma_p_half", "mma_p_full", "mma_qk_next", "kv_landed"):  # leader only
         assert (ev[0, :, E[name]]["globaltimer_ns"] > 0).all(), name
-    # wait-site counts: 2 clusters = 4 CTAs, 64 KV tiles per unit, one unit per cluster
+    # the segment timeline has cluster 0's one segment: unit 0, 64 tiles
+    assert int(seg[0, 0, 3]) == 0 * 65536 + 64 and seg[0, 0, 0] > 0
+    assert not wait.any()  # no wait statistics below trace level 2
+
+
+def test_waitstats_build_statistics():
+    """Per-wait-site statistics: the counts stay within the hand-offs the schedule has
+    (4 CTAs, 64 KV tiles per unit, one unit per cluster), the softmax warps wait for S,
+    and every share of a role's time lies in [0, 1]."""
+    h = _lib.load(build_variant("waitstats"))
+    assert _lib.build_config(h)["trace"] == 2
+    ev, seg, wait = _traced_forward(h, TRACE_CFG)
+    assert trace.check_chain(ev) == []
     n_kv, ctas, leaders = 64, 4, 2
     assert int(wait[0, 1]) == ctas
-    assert int(wait[6, 1]) == ctas * 8 * n_kv          # softmax: S(j) of its tile
-    assert int(wait[7, 1]) == ctas * 4 * 2 * n_kv      # correction: both tiles' rescale factor
-    assert int(wait[5, 1]) == leaders * 4 * n_kv       # MMA: P half + P full of both tiles
-    assert int(wait[2, 1]) == ctas * 2 * n_kv          # producer: K and V stage per tile
-    assert int(wait[3, 1]) == leaders * 2              # MMA: both Q tiles of the unit
+    assert 0 < int(wait[6, 1]) <= ctas * 8 * n_kv      # softmax: S(j) of its tile
+    assert int(wait[7, 1]) <= ctas * 4 * 2 * n_kv      # correction: both tiles' rescale factor
+    assert int(wait[5, 1]) <= leaders * 4 * n_kv       # MMA: P half + P full of both tiles
+    assert int(wait[2, 1]) <= ctas * 2 * n_kv          # producer: K and V stage per tile
+    assert int(wait[3, 1]) <= leaders * 2              # MMA: both Q tiles of the unit
     rows = trace.wait_table(wait, trace.clock_ghz(ev))
-    assert all(0.0 <= r["share_of_role_time"] <= 1.0 for r in rows), rows
-    # the segment timeline has cluster 0's one segment: unit 0, 64 tiles
-    assert int(seg[0, 0, 3]) == 0 * 65536 + n_kv and seg[0, 0, 0] > 0
+    assert rows and all(0.0 <= r["share_of_role_time"] <= 1.0 for r in rows), rows
 
 
 @pytest.mark.parametrize("rung,code", [("floor", 1), ("faux", 2), ("noexp", 3)])
