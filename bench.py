@@ -71,6 +71,9 @@ def parse_args():
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--validate", action="store_true", help="NCCL-gather O to rank 0 afterwards")
     ap.add_argument("--cpu-seconds", type=float, default=10.0, help="CPU baseline sample budget")
+    ap.add_argument("--heads", type=int, default=None,
+                    help="run only the first N heads of the configuration (a smaller case of the "
+                         "same kernel, for profiling; the line's config says so)")
     ap.add_argument("--sweep", action="store_true",
                     help="time this kernel and the reference kernel on the reference's published "
                          "single-head shapes and on multi-wave ones (one JSON line per shape)")
@@ -306,6 +309,8 @@ def run_ours(args, cfg, world, rank, local):
         ha.synchronize()
         if world > 1:
             dist.barrier()
+        e2e_sampler = ClockSampler(local)
+        e2e_sampler.start()
         e_start, e_end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         e_start.record(ha.s_in)
         for i in range(args.steps):
@@ -315,7 +320,7 @@ def run_ours(args, cfg, world, rank, local):
         torch.cuda.synchronize(dev)
         e2e_ms = e_start.elapsed_time(e_end) / args.steps
         e2e = {"ms": e2e_ms, "h2d": sum(t.numel() * t.element_size() for t in (q_h, k_h, v_h)),
-               "d2h": o.numel() * o.element_size(), "bw": bw}
+               "d2h": o.numel() * o.element_size(), "bw": bw, "clocks": e2e_sampler.stop()}
 
     # max over ranks
     if world > 1:
@@ -391,7 +396,11 @@ def run_ours(args, cfg, world, rank, local):
                        "copy_roofline": {"h2d_gbs": e2e["bw"]["h2d_gbs"],
                                          "d2h_gbs": e2e["bw"]["d2h_gbs"],
                                          "bound_ms": round(bound_ms, 4),
-                                         "frac": round(bound_ms / e2e_ms_max, 4)}}
+                                         "frac": round(bound_ms / e2e_ms_max, 4)},
+                       # copies and kernels back to back, with no idle gap: the clocks the
+                       # kernels ran at (under the power cap they can sit below the timed
+                       # steps' clocks, which `bound_ms` assumes)
+                       "clocks": e2e["clocks"]}
         line["gpu_launches"] += args.steps * plan["kernels"]
     if world == 1 and not args.no_cpu_baseline:
         line["cpu_baseline"] = cpu_baseline(cfg, args.cpu_seconds)
@@ -597,8 +606,14 @@ def main():
     if world != args.gpus:
         print(f"# note: --gpus {args.gpus} but WORLD_SIZE={world}; using WORLD_SIZE",
               file=sys.stderr)
+    import dataclasses
+
     from llm_fa_b200.workloads import CONFIGS
     cfg = CONFIGS[args.config]
+    if args.heads is not None:
+        if not 1 <= args.heads <= cfg.heads:
+            raise SystemExit(f"--heads must be in 1..{cfg.heads}")
+        cfg = dataclasses.replace(cfg, heads=args.heads)
     import torch.distributed as dist
     if world > 1:
         import torch

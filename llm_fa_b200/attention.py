@@ -8,7 +8,9 @@ the sm_100a kernel in libllm_fa_b200.so.
 """
 from __future__ import annotations
 
+import contextlib
 import ctypes
+import functools
 import math
 
 import torch
@@ -84,26 +86,31 @@ def forward_with(handle, q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, *,
             raise RuntimeError(f"out shape {tuple(out.shape)} must equal Q shape {tuple(q.shape)}")
     o4 = _as_bshd(out, "out")
     scale = (1.0 / math.sqrt(HEAD_DIM)) if softmax_scale is None else float(softmax_scale)
-    with torch.cuda.device(device):
+    # the library launches on the current device: switch only when the tensors live elsewhere
+    ctx = (torch.cuda.device(device) if device.index != torch.cuda.current_device()
+           else contextlib.nullcontext())
+    with ctx:
         # scratch for split KV ranges, from the caching allocator on this stream
         ws_bytes = workspace_size(device) if split_kv else 0
         ws = torch.empty(ws_bytes, dtype=torch.uint8, device=device) if split_kv else None
         stream = torch.cuda.current_stream(device).cuda_stream
         lse = torch.empty(B, H, Sq, dtype=torch.float32, device=device) if return_lse else None
         rc = handle.llmfa_forward_lse(
-            ctypes.c_void_p(q4.data_ptr()), _lib.strides3(q4.stride()[:3]),
-            ctypes.c_void_p(k4.data_ptr()), _lib.strides3(k4.stride()[:3]),
-            ctypes.c_void_p(v4.data_ptr()), _lib.strides3(v4.stride()[:3]),
-            ctypes.c_void_p(o4.data_ptr()), _lib.strides3(o4.stride()[:3]),
-            ctypes.c_void_p(lse.data_ptr() if return_lse else None),
-            _lib.strides2((H * Sq, Sq)),
-            B, H, Sq, Sk, ctypes.c_float(scale),
-            ctypes.c_void_p(ws.data_ptr() if ws is not None else None), ws_bytes,
-            ctypes.c_void_p(stream))
+            q4.data_ptr(), _strides3(q4.stride()), k4.data_ptr(), _strides3(k4.stride()),
+            v4.data_ptr(), _strides3(v4.stride()), o4.data_ptr(), _strides3(o4.stride()),
+            lse.data_ptr() if return_lse else None, _lib.strides2((H * Sq, Sq)),
+            B, H, Sq, Sk, scale, ws.data_ptr() if ws is not None else None, ws_bytes, stream)
     _lib.check(rc, "llmfa_forward_lse")
     if return_lse:
         return out, (lse if q.dim() == 4 else lse.reshape(Sq))
     return out
+
+
+@functools.lru_cache(maxsize=256)
+def _strides3(stride: tuple) -> ctypes.Array:
+    """(batch, seq, head) element strides of a [B, S, H, 128] view, as the C array type
+    (cached: a loop of calls on the same views reuses the converted array)."""
+    return _lib.strides3(stride[:3])
 
 
 _WS_BYTES: dict[int, int] = {}

@@ -23,6 +23,19 @@ import torch
 from .attention import HEAD_DIM, attention_forward
 
 
+class _Slot:
+    """One set of device buffers and the events that order its reuse."""
+
+    def __init__(self, q_shape, kv_shape, device):
+        mk = lambda shape: torch.empty(shape, dtype=torch.bfloat16, device=device)  # noqa: E731
+        self.key = (q_shape, kv_shape)
+        self.q, self.k, self.v, self.o = mk(q_shape), mk(kv_shape), mk(kv_shape), mk(q_shape)
+        self.copied_in = torch.cuda.Event()
+        self.computed = torch.cuda.Event()
+        self.copied_out = torch.cuda.Event()
+        self.used = False
+
+
 class HostAttention:
     """Pipelined attention_forward for host (CPU) tensors; see the module docstring."""
 
@@ -36,16 +49,25 @@ class HostAttention:
             self.s_in = torch.cuda.Stream(self.device)
             self.s_compute = torch.cuda.Stream(self.device)
             self.s_out = torch.cuda.Stream(self.device)
-        self._slots: list[dict | None] = [None] * depth
+        self._slots: list[_Slot | None] = [None] * depth
         self._n = 0
 
-    def _slot(self, i: int, q, k, v):
+    def _slot(self, i: int, q, k) -> _Slot:
         key = (tuple(q.shape), tuple(k.shape))
         slot = self._slots[i]
-        if slot is None or slot["key"] != key:
-            mk = lambda t: torch.empty(t.shape, dtype=torch.bfloat16, device=self.device)  # noqa: E731
-            slot = {"key": key, "q": mk(q), "k": mk(k), "v": mk(v), "o": mk(q),
-                    "computed": None, "copied_out": None}
+        if slot is None or slot.key != key:
+            if slot is not None:
+                # The old buffers come from the caching allocator on the current stream;
+                # work queued on the three streams may still use them, so they must not be
+                # handed out again before it has finished.
+                for buf, streams in ((slot.q, (self.s_in, self.s_compute)),
+                                     (slot.k, (self.s_in, self.s_compute)),
+                                     (slot.v, (self.s_in, self.s_compute)),
+                                     (slot.o, (self.s_compute, self.s_out))):
+                    for st in streams:
+                        buf.record_stream(st)
+            with torch.cuda.device(self.device):
+                slot = _Slot(key[0], key[1], self.device)
             self._slots[i] = slot
         return slot
 
@@ -66,46 +88,37 @@ class HostAttention:
             self._check(t, nm)
         if out.shape != q.shape:
             raise RuntimeError(f"out shape {tuple(out.shape)} must equal Q shape {tuple(q.shape)}")
-        i = self._n % self.depth
+        if k.shape != v.shape:
+            raise RuntimeError(f"K {tuple(k.shape)} and V {tuple(v.shape)} must have the same shape")
+        slot = self._slot(self._n % self.depth, q, k)
         self._n += 1
-        slot = self._slot(i, q, k, v)
+        s_in, s_c, s_out = self.s_in, self.s_compute, self.s_out
         with torch.cuda.device(self.device):
             # copy in, once the compute that last read this slot's inputs is done
-            if slot["computed"] is not None:
-                self.s_in.wait_event(slot["computed"])
-            with torch.cuda.stream(self.s_in):
-                slot["q"].copy_(q, non_blocking=True)
-                slot["k"].copy_(k, non_blocking=True)
-                slot["v"].copy_(v, non_blocking=True)
-                copied_in = torch.cuda.Event()
-                copied_in.record(self.s_in)
+            if slot.used:
+                s_in.wait_event(slot.computed)
+            with torch.cuda.stream(s_in):
+                slot.q.copy_(q, non_blocking=True)
+                slot.k.copy_(k, non_blocking=True)
+                slot.v.copy_(v, non_blocking=True)
+            slot.copied_in.record(s_in)
             # compute, once the inputs landed and the slot's last output was copied out
-            self.s_compute.wait_event(copied_in)
-            if slot["copied_out"] is not None:
-                self.s_compute.wait_event(slot["copied_out"])
-            with torch.cuda.stream(self.s_compute):
-                attention_forward(slot["q"], slot["k"], slot["v"], out=slot["o"],
+            s_c.wait_event(slot.copied_in)
+            if slot.used:
+                s_c.wait_event(slot.copied_out)
+            with torch.cuda.stream(s_c):
+                attention_forward(slot.q, slot.k, slot.v, out=slot.o,
                                   softmax_scale=softmax_scale)
-                computed = torch.cuda.Event()
-                computed.record(self.s_compute)
+            slot.computed.record(s_c)
             # copy out
-            self.s_out.wait_event(computed)
-            with torch.cuda.stream(self.s_out):
-                out.copy_(slot["o"], non_blocking=True)
-                copied_out = torch.cuda.Event()
-                copied_out.record(self.s_out)
-            # The slot's buffers come from the caching allocator on the current
-            # stream; when a later request of another shape replaces them, they
-            # must not be handed out again before this work on the three
-            # streams has finished.
-            for name, streams in (("q", (self.s_in, self.s_compute)),
-                                  ("k", (self.s_in, self.s_compute)),
-                                  ("v", (self.s_in, self.s_compute)),
-                                  ("o", (self.s_compute, self.s_out))):
-                for st in streams:
-                    slot[name].record_stream(st)
-        slot["computed"], slot["copied_out"] = computed, copied_out
-        return copied_out
+            s_out.wait_event(slot.computed)
+            with torch.cuda.stream(s_out):
+                out.copy_(slot.o, non_blocking=True)
+            slot.copied_out.record(s_out)
+            done = torch.cuda.Event()
+            done.record(s_out)
+        slot.used = True
+        return done
 
     def synchronize(self) -> None:
         """Wait until every submitted request's output is in host memory."""
