@@ -55,7 +55,8 @@ PUBLISHED_REF_TFLOPS = {"c2": 362.5, "c3": 810.6}
 # kernel ends), not a measurement of the timed steps.
 PROFILED_TRAFFIC_BYTES: dict[str, float | None] = {
     "c2": 12.66e6,
-    "c3": 142.6e6,
+    "c3": 160.3e6,
+    "c4": 1055.4e6,
 }
 L2_FLUSH_BYTES = 256 << 20
 
