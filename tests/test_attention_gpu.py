@@ -449,3 +449,35 @@ def test_cuda_graph_capture_and_replay(B, H, Sq, Sk):
         torch.cuda.synchronize()
         assert device_status() == 0
         assert torch.equal(o, attention_forward(q, k, v))
+
+
+# ----------------------------------------------------------------- launch-spec cache
+def test_launch_spec_cache_keys_on_every_argument():
+    """The launcher caches tensor maps and launch plans per argument set: calls that differ
+    only in buffers, in the output view's strides or in the softmax scale must each get
+    their own (more than the cache's eight entries, interleaved and repeated)."""
+    cfgs = [Config("lc", 1, 2, 700 + 64 * i, 900, seed=40 + i) for i in range(3)]
+    cases = []
+    for cfg in cfgs:
+        q, k, v = make_inputs(cfg)
+        cases.append((cfg, q, k, v, q.cuda(), k.cuda(), v.cuda()))
+    outs = {}
+    for rep in range(2):
+        for i, (cfg, q, k, v, qd, kd, vd) in enumerate(cases):
+            for scale in (None, 0.05):
+                o = attention_forward(qd, kd, vd, softmax_scale=scale)
+                store = torch.zeros(1, cfg.seq_q, 2, 256, dtype=torch.bfloat16, device="cuda")
+                o_strided = store[..., :128]
+                attention_forward(qd, kd, vd, softmax_scale=scale, out=o_strided)
+                torch.cuda.synchronize()
+                assert torch.equal(o, o_strided)
+                if rep == 0:
+                    outs[(i, scale)] = o.cpu()
+                    _assert_close(o.cpu(), sdpa_fp32(q, k, v, scale))
+                else:
+                    assert torch.equal(o.cpu(), outs[(i, scale)])
+    # same buffers, new contents: the cached maps address the data, not a copy of it
+    cfg, q, k, v, qd, kd, vd = cases[0]
+    q2, k2, v2 = make_inputs(Config("lc2", 1, 2, cfg.seq_q, 900, seed=99))
+    qd.copy_(q2); kd.copy_(k2); vd.copy_(v2)
+    _assert_close(attention_forward(qd, kd, vd).cpu(), sdpa_fp32(q2, k2, v2))
