@@ -78,10 +78,18 @@ def build_variant(name: str, force: bool = False, verbose: bool = False) -> Path
     return _compile(variant_path(name), VARIANTS[name], force, verbose)
 
 
+def build_all(force: bool = False, verbose: bool = False) -> list[Path]:
+    """The product library and every variant, compiled concurrently (one nvcc each)."""
+    import concurrent.futures
+    jobs = [(LIB, [])] + [(variant_path(n), d) for n, d in VARIANTS.items()]
+    with concurrent.futures.ThreadPoolExecutor(max_workers=len(jobs)) as pool:
+        return list(pool.map(lambda j: _compile(j[0], j[1], force, verbose), jobs))
+
+
 def _compile(lib: Path, defines: list[str], force: bool, verbose: bool) -> Path:
     if not force and not is_stale(lib):
         return lib
-    tmp = lib.with_suffix(".so.tmp")
+    tmp = lib.with_name(lib.name + f".{os.getpid()}.tmp")
     cmd = [nvcc_path(), *NVCC_FLAGS, *defines, "-o", str(tmp), *map(str, SOURCES)]
     proc = subprocess.run(cmd, capture_output=True, text=True)
     if verbose or proc.returncode != 0:

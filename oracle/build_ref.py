@@ -90,14 +90,22 @@ def build(ref_dir: Path, name: str = "llm_fa_ref", verbose: bool = False) -> Pat
 def build_if_possible() -> Path | None:
     """Build every reference module that is missing, when the reference checkout is
     present; returns the llm_fa_ref module path (or None)."""
+    import concurrent.futures
+    import multiprocessing
+
     ref = reference_dir()
-    for name, (source, _, _) in REF_MODULES.items():
-        if built_module_path(name) is not None or ref is None or not (ref / source).exists():
-            continue
-        try:
-            build(ref, name)
-        except Exception as exc:  # the comparison baselines are optional; the product is not
-            sys.stderr.write(f"reference module {name} not built: {exc}\n")
+    todo = [name for name, (source, _, _) in REF_MODULES.items()
+            if built_module_path(name) is None and ref is not None and (ref / source).exists()]
+    if todo:
+        # one process per module (each is a separate extension build in its own directory)
+        with concurrent.futures.ProcessPoolExecutor(
+                max_workers=len(todo), mp_context=multiprocessing.get_context("spawn")) as pool:
+            futures = {name: pool.submit(build, ref, name) for name in todo}
+            for name, fut in futures.items():
+                try:
+                    fut.result()
+                except Exception as exc:  # the comparison baselines are optional; the product is not
+                    sys.stderr.write(f"reference module {name} not built: {exc}\n")
     return built_module_path("llm_fa_ref")
 
 
