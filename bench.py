@@ -24,6 +24,11 @@ device inside every call, so stream events cannot bracket its kernel alone).
 Its `e2e` takes the same host-data path as this arm's: pinned Q/K/V copied in,
 the call, O copied back, every step. When that module is absent it times the
 reference's CPU oracle path (fp32 SDPA, validate.py:19-27) instead.
+
+On one GPU this arm's line also carries `same_box_library`: flashinfer's CUTLASS
+Blackwell FMHA (baseline/library_fmha.py, prebuilt offline) on the same inputs,
+timed the same way after this arm (FA4 itself is not installed in this image),
+or why it is unavailable.
 """
 from __future__ import annotations
 
@@ -224,6 +229,36 @@ def gather_floats(value: float, dev) -> list[float]:
     return [float(p[0]) for p in parts]
 
 
+def time_library(q, k, v, ours_out, flops: int, args, flush, ours_ms: float) -> dict:
+    """flashinfer's CUTLASS Blackwell FMHA (baseline/library_fmha.py) on the same inputs and
+    GPU, timed like this arm (warm-up, L2 flush before every call, CUDA events): a
+    same-box library comparison beside the line, not part of `value`."""
+    import torch
+    try:
+        from baseline.library_fmha import LibraryFMHA
+        fmha = LibraryFMHA(q, k, v, 1.0 / 128 ** 0.5)
+    except Exception as e:  # not built, or flashinfer missing: say so
+        return {"unavailable": f"{type(e).__name__}: {e}"[:240]}
+    for _ in range(max(args.warmup, 3)):
+        flush.zero_()
+        fmha()
+    starts = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
+    ends = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
+    for i in range(args.steps):
+        flush.zero_()
+        starts[i].record()
+        fmha()
+        ends[i].record()
+    torch.cuda.synchronize()
+    ms = statistics.fmean(s.elapsed_time(e) for s, e in zip(starts, ends))
+    diff = (fmha.out.float() - ours_out.float()).abs().max().item()
+    return {"impl": fmha.version, "value": round(flops / (ms / 1e3) / 1e12, 2), "unit": UNIT,
+            "ms_per_step": round(ms, 5), "speedup_of_this_arm": round(ms / ours_ms, 3),
+            "max_abs_diff_vs_this_arm": diff,
+            "note": "FA4 (flash_attn.cute) is not installed in this image; this is the "
+                    "tcgen05 attention kernel that is, timed after this arm"}
+
+
 def clocks_from_samplers(*clocks):
     got = [c for c in clocks if c]
     return got[0] if got else None
@@ -403,6 +438,8 @@ def run_ours(args, cfg, world, rank, local):
                        # steps' clocks, which `bound_ms` assumes)
                        "clocks": e2e["clocks"]}
         line["gpu_launches"] += args.steps * plan["kernels"]
+    if world == 1:
+        line["same_box_library"] = time_library(q, k, v, o, flops_local, args, flush, mean_ms)
     if world == 1 and not args.no_cpu_baseline:
         line["cpu_baseline"] = cpu_baseline(cfg, args.cpu_seconds)
     return line
@@ -555,7 +592,8 @@ def run_sweep(args) -> None:
     """This kernel and the reference's llm_fa.cu kernel (oracle/_ref) on the same GPU, on
     the sweep shapes: CUDA events around each call, a 256 MiB L2 flush before every call,
     median of --steps calls after --warmup; also the largest difference between the two
-    outputs."""
+    outputs. Where baseline/library_fmha.py's prebuilt library kernel exists, it is timed
+    the same way beside them."""
     import torch
 
     from llm_fa_b200 import attention_forward, device_status
@@ -587,12 +625,27 @@ def run_sweep(args) -> None:
         t_ref = median_us(lambda: mod.llm_fa_forward(Q, K, V))
         diff = (O.float() - mod.llm_fa_forward(Q, K, V)[0].float()).abs().max().item()
         flops = 4 * q_len * sk * 128
-        print(json.dumps({"q": q_len, "sk": sk, "ours_us": round(t_ours, 1),
-                          "reference_us": round(t_ref, 1),
-                          "speedup": round(t_ref / t_ours, 3),
-                          "ours_tflops": round(flops / t_ours / 1e6, 1),
-                          "reference_tflops": round(flops / t_ref / 1e6, 1),
-                          "max_abs_diff_vs_reference": diff}), flush=True)
+        row = {"q": q_len, "sk": sk, "ours_us": round(t_ours, 1),
+               "reference_us": round(t_ref, 1),
+               "speedup": round(t_ref / t_ours, 3),
+               "ours_tflops": round(flops / t_ours / 1e6, 1),
+               "reference_tflops": round(flops / t_ref / 1e6, 1),
+               "max_abs_diff_vs_reference": diff}
+        # the same-box library kernel (baseline/library_fmha.py), when built
+        try:
+            from baseline.library_fmha import LibraryFMHA
+            fmha = LibraryFMHA(*(t.view(1, -1, 1, 128) for t in (Q, K, V)), 1.0 / 128 ** 0.5)
+        except Exception as e:
+            row["library"] = {"unavailable": f"{type(e).__name__}: {e}"[:160]}
+        else:
+            t_lib = median_us(fmha)
+            row["library"] = {"impl": fmha.version, "us": round(t_lib, 1),
+                              "tflops": round(flops / t_lib / 1e6, 1),
+                              "speedup_of_this_kernel": round(t_lib / t_ours, 3),
+                              "max_abs_diff_vs_this_kernel":
+                                  (fmha.out.view(q_len, 128).float() - O.float()).abs().max().item()}
+            del fmha
+        print(json.dumps(row), flush=True)
         del Q, K, V, O
     if device_status() != 0:
         raise RuntimeError(f"device status {device_status()}")
