@@ -59,11 +59,17 @@ def variant_path(name: str) -> Path:
     return PKG / f"libllm_fa_b200_{name}.so"
 
 
-def is_stale(lib: Path = LIB) -> bool:
+# The tensor-core rate microbenchmark (llm_fa_b200.mma_rate): its own source and library.
+MMARATE_LIB = PKG / "libllm_fa_b200_mmarate.so"
+MMARATE_SOURCES = [CSRC / "mma_rate.cu"]
+MMARATE_DEPS = MMARATE_SOURCES + [CSRC / "ptx.cuh"]
+
+
+def is_stale(lib: Path = LIB, deps: list[Path] = DEPS) -> bool:
     if not lib.exists():
         return True
     t = lib.stat().st_mtime
-    return any(d.stat().st_mtime > t for d in DEPS)
+    return any(d.stat().st_mtime > t for d in deps)
 
 
 def build(force: bool = False, verbose: bool = False) -> Path:
@@ -78,28 +84,40 @@ def build_variant(name: str, force: bool = False, verbose: bool = False) -> Path
     return _compile(variant_path(name), VARIANTS[name], force, verbose)
 
 
+def build_mmarate(force: bool = False, verbose: bool = False) -> Path:
+    """Compile the tensor-core rate microbenchmark library if missing or stale."""
+    return _compile(MMARATE_LIB, [], force, verbose, MMARATE_SOURCES, MMARATE_DEPS)
+
+
 def build_all(force: bool = False, verbose: bool = False) -> list[Path]:
-    """The product library and every variant, compiled concurrently (one nvcc each)."""
+    """The product library, every variant and the microbenchmark, compiled concurrently
+    (one nvcc each)."""
     import concurrent.futures
-    jobs = [(LIB, [])] + [(variant_path(n), d) for n, d in VARIANTS.items()]
+    jobs = [(LIB, [], SOURCES, DEPS)] + [(variant_path(n), d, SOURCES, DEPS)
+                                         for n, d in VARIANTS.items()]
+    jobs.append((MMARATE_LIB, [], MMARATE_SOURCES, MMARATE_DEPS))
     with concurrent.futures.ThreadPoolExecutor(max_workers=len(jobs)) as pool:
-        return list(pool.map(lambda j: _compile(j[0], j[1], force, verbose), jobs))
+        return list(pool.map(lambda j: _compile(j[0], j[1], force, verbose, j[2], j[3]), jobs))
 
 
-def _compile(lib: Path, defines: list[str], force: bool, verbose: bool) -> Path:
-    if not force and not is_stale(lib):
+def _compile(lib: Path, defines: list[str], force: bool, verbose: bool,
+             sources: list[Path] = SOURCES, deps: list[Path] = DEPS) -> Path:
+    if not force and not is_stale(lib, deps):
         return lib
     tmp = lib.with_name(lib.name + f".{os.getpid()}.tmp")
-    cmd = [nvcc_path(), *NVCC_FLAGS, *defines, "-o", str(tmp), *map(str, SOURCES)]
+    cmd = [nvcc_path(), *NVCC_FLAGS, *defines, "-o", str(tmp), *map(str, sources)]
     proc = subprocess.run(cmd, capture_output=True, text=True)
     if verbose or proc.returncode != 0:
         sys.stderr.write(proc.stdout + proc.stderr)
     if proc.returncode != 0:
         raise RuntimeError(f"nvcc failed ({proc.returncode}): {' '.join(cmd)}")
-    # ptxas -v: the attention kernel must not spill
+    # ptxas -v: report every kernel that spills, by name
+    entry = "?"
     for line in (proc.stdout + proc.stderr).splitlines():
-        if "spill stores" in line and not line.strip().startswith("0 bytes stack frame, 0 bytes spill"):
-            sys.stderr.write(f"warning: register spills reported by ptxas: {line.strip()}\n")
+        if "Compiling entry function" in line:
+            entry = line.split("'")[1] if "'" in line else line.strip()
+        elif "spill stores" in line and not line.strip().startswith("0 bytes stack frame, 0 bytes spill"):
+            sys.stderr.write(f"warning: {lib.name}: {entry}: ptxas reports {line.strip()}\n")
     os.replace(tmp, lib)
     return lib
 
